@@ -1,0 +1,468 @@
+"""Benchmark of the Zealot attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload: one paged-decode attention step of a
+Llama-3-8B layer -- 64 sequences per GPU, 32 query / 8 kv heads, head_dim 128,
+bf16, context U[512, 4096], block_size 16, block tables drawn from a seeded
+random permutation of a 65536-block pool, q/K/V ~ N(0, 1). A step is one
+zl_paged_decode launch over every sequence; tokens/s = sequences / step time.
+
+Multi-GPU (torchrun, one process per GPU): kv-head-group sharding, weak
+scaling -- at N GPUs the job is 64*N sequences and rank r owns kv heads
+[r*8/N, (r+1)*8/N) (and their query heads) of all of them, so every rank moves
+the same bytes as the 1-GPU step and no collective touches the data path.
+
+The JSON line carries value (device-resident inputs), e2e (through the C ABI
+with pinned host buffers copied in and out inside the timed region), the
+roofline of the decode kernel, side measurements of the C3 prefill and
+reshape_and_cache, sampled clocks, and the CPU baseline (the oracle, a C
+restatement of the reference CPU attention). `--impl reference` times that
+oracle alone, multi-threaded on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B_PER_GPU, H, HKV, D, BS, NUM_BLOCKS, MAX_BLOCKS = 64, 32, 8, 128, 16, 65536, 256
+CTX_LO, CTX_HI = 512, 4096
+SEED = 2024
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ workload
+
+def make_lens_tables(world: int):
+    """Context lengths and block tables of the global batch (identical on every rank)."""
+    rng = np.random.default_rng(SEED)
+    B = B_PER_GPU * world
+    lens = rng.integers(CTX_LO, CTX_HI + 1, size=B).astype(np.int32)
+    nblk = (lens + BS - 1) // BS
+    # per rank the pool holds 65536 blocks of its own kv heads; the tables index it
+    pool_blocks = max(NUM_BLOCKS, int(nblk.sum()))
+    perm = rng.permutation(pool_blocks).astype(np.int32)
+    tables = np.full((B, MAX_BLOCKS), -1, np.int32)
+    off = 0
+    for b in range(B):
+        tables[b, : nblk[b]] = perm[off: off + nblk[b]]
+        off += nblk[b]
+    return lens, tables, pool_blocks
+
+
+def algorithmic_bytes(lens, hkv, h, esize=2):
+    """Bytes one decode step must move: K and V of every context token of every kv
+    head, q in, out, block-table entries and seq_lens."""
+    nblk = (lens.astype(np.int64) + BS - 1) // BS
+    kv = int(lens.astype(np.int64).sum()) * hkv * D * 2 * esize
+    qo = len(lens) * h * D * 2 * esize
+    return kv + qo + int(nblk.sum()) * 4 + len(lens) * 4
+
+
+# -------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------- ours
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import zealot_b200 as zb
+    from zealot_b200.context import ptr
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", dev))
+
+    lens, tables, pool_blocks = make_lens_tables(world)
+    B = len(lens)
+    hkv_l, h_l = HKV // world, H // world  # this rank's kv-head group
+    assert HKV % world == 0, "kv heads must divide over the GPUs"
+    ctx = zb.GpuContext(dev)
+    attn = zb.CudaAttention(ctx)
+    stream = torch.cuda.Stream(dev)
+    g = torch.Generator(device="cuda").manual_seed(SEED + rank)
+    with torch.cuda.stream(stream):
+        kpool = torch.randn((pool_blocks, hkv_l, BS, D), generator=g, device="cuda").to(torch.bfloat16)
+        vpool = torch.randn((pool_blocks, hkv_l, BS, D), generator=g, device="cuda").to(torch.bfloat16)
+        q = torch.randn((B, h_l, D), generator=g, device="cuda").to(torch.bfloat16)
+        out = torch.empty_like(q)
+        t_tab = torch.from_numpy(tables).cuda()
+        t_len = torch.from_numpy(lens).cuda()
+    stream.synchronize()
+    s_handle = stream.cuda_stream
+
+    def step():
+        attn.paged_forward(q, kpool, vpool, t_tab, t_len, out, B, h_l, hkv_l, D, BS, MAX_BLOCKS,
+                           num_blocks=pool_blocks, stream=s_handle)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    for _ in range(args.warmup):
+        step()
+    ctx.check_status(s_handle)
+    clocks = ClockSampler(dev)
+    barrier()
+    clocks.start()
+    # ~1 s of back-to-back steps so the sampler sees the GPU under this load; the
+    # timed K steps follow immediately, inside the same sampling window.
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:
+        for _ in range(20):
+            step()
+        stream.synchronize()
+    barrier()
+    launches0 = ctx.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    dev_ms = e0.elapsed_time(e1)
+    launches = ctx.launch_count() - launches0
+    clk = clocks.stop()
+    ctx.check_status(s_handle)
+    ms_step = max_over_ranks(dev_ms / args.steps)
+
+    # ---- end to end through the C ABI with pinned host buffers
+    from zealot_b200 import lib
+    hq = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
+    hq.copy_(q.cpu())
+    htab = torch.from_numpy(tables).pin_memory()
+    hlen = torch.from_numpy(lens).pin_memory()
+    hout = torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True)
+    dq, dtab, dlen, dout = torch.empty_like(q), torch.empty_like(t_tab), torch.empty_like(t_len), torch.empty_like(out)
+    nbytes = lambda t: t.numel() * t.element_size()
+    h2d = nbytes(hq) + nbytes(htab) + nbytes(hlen)
+    d2h = nbytes(hout)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dtab.copy_(htab, non_blocking=True)
+        dlen.copy_(hlen, non_blocking=True)
+        rc = lib.zl_paged_decode(ctx.handle, ptr(dq), ptr(kpool), ptr(vpool), ptr(dtab), ptr(dlen),
+                                 ptr(dout), B, h_l, hkv_l, D, BS, MAX_BLOCKS, pool_blocks, 0.0, 0, 0, 1,
+                                 s_handle)
+        assert rc == 0
+        hout.copy_(dout, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        l0 = ctx.launch_count()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_launches = ctx.launch_count() - l0
+    ctx.check_status(s_handle)
+
+    # ---- roofline of the decode kernel (one launch per step)
+    peaks = load_peaks()
+    alg = algorithmic_bytes(lens, hkv_l, h_l)
+    achieved = alg / (dev_ms / args.steps * 1e-3) / 1e9
+    traffic = load_traffic("decode_c2")
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+            "algorithmic_bytes": alg, "peak_source": peaks["source"]}
+
+    side = {}
+    if rank == 0 and world == 1 and not args.no_side:
+        del kpool, vpool
+        torch.cuda.empty_cache()
+        side = side_measurements(ctx, attn, stream, peaks, args)
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        tokens_per_s = B / (ms_step * 1e-3)
+        line = {
+            "metric": "paged_decode_tokens_per_s",
+            "value": round(tokens_per_s, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/K/V, U[512,4096] contexts, random-permutation block tables)",
+            "config": {"workload": "C2 paged decode, Llama-3-8B layer shape: 32 q / 8 kv heads, head_dim 128, "
+                                   "bf16, block_size 16, 65536-block pool per GPU",
+                       "global_batch": B, "per_gpu_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                       "parallelism": f"kv-head groups x{world} (rank r: kv heads [r*{HKV // world}, "
+                                      f"(r+1)*{HKV // world}))",
+                       "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"},
+            "hbm_gbs": round(achieved, 1),
+            "hbm_frac": round(achieved / peaks["hbm_gbs"], 4),
+            "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "zl_paged_decode (C ABI) with pinned host q/tables/seq_lens in, out back"},
+            "gpu_launches": int(launches),
+            "e2e_gpu_launches": int(e2e_launches),
+            "roofline": roof,
+            "clocks": clk,
+        }
+        line.update(side)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_single(lens, tables)
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def side_measurements(ctx, attn, stream, peaks, args):
+    """C3 prefill TFLOPS and reshape_and_cache GB/s (1 GPU, same run)."""
+    import torch
+    res = {}
+    rng = np.random.default_rng(3)
+    lens = rng.integers(256, 8193, size=16)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    g = torch.Generator(device="cuda").manual_seed(3)
+    with torch.cuda.stream(stream):
+        q = torch.randn((T, H, D), generator=g, device="cuda").to(torch.bfloat16)
+        k = torch.randn((T, HKV, D), generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn((T, HKV, D), generator=g, device="cuda").to(torch.bfloat16)
+        o = torch.empty_like(q)
+        tcu = torch.from_numpy(cu).cuda()
+    sh = stream.cuda_stream
+    flops = sum(4 * H * D * int(L) * (int(L) + 1) / 2 for L in lens)
+
+    def pre():
+        attn.forward_gpu(q, k, v, tcu, o, H, HKV, D, int(lens.max()), causal=True, stream=sh)
+
+    n = 5
+    for _ in range(3):
+        pre()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        pre()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    tf = flops / (ms * 1e-3) / 1e12
+    res["prefill"] = {"workload": "C3 varlen causal prefill: 16 seqs, L U[256,8192], 32/8 heads, d 128, bf16",
+                      "ms": round(ms, 4), "tflops": round(tf, 2), "peak_tflops": peaks["bf16_tflops"],
+                      "frac": round(tf / peaks["bf16_tflops"], 4), "flop": flops}
+    # reshape_and_cache of the same tokens into a pool via a random slot mapping
+    nb = (T + BS - 1) // BS + 64
+    with torch.cuda.stream(stream):
+        pk = torch.empty((nb, HKV, BS, D), dtype=torch.bfloat16, device="cuda")
+        pv = torch.empty_like(pk)
+        slots = torch.from_numpy(rng.permutation(nb * BS)[:T].astype(np.int64)).cuda()
+    for _ in range(3):
+        attn.reshape_and_cache(k, v, pk, pv, slots, HKV, D, BS, nb, stream=sh)
+    e0.record(stream)
+    for _ in range(n):
+        attn.reshape_and_cache(k, v, pk, pv, slots, HKV, D, BS, nb, stream=sh)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    byts = 2 * (T * HKV * D * 2) * 2 + 8 * T
+    res["reshape_and_cache"] = {"workload": f"C3 tokens ({T}) x 8 kv heads x 128 bf16, random slots",
+                                "ms": round(ms, 4), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+                                "frac": round(byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+    ctx.check_status(sh)
+    return res
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic(name):
+    p = os.path.join(ROOT, "profiles", f"{name}_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+# ------------------------------------------------------------- CPU baselines
+
+def _oracle_inputs(lens, tables, hkv, h, n_seqs):
+    """fp32 host copies of a sample of the workload, pool compacted to the referenced blocks."""
+    from oracle import oracle
+    rng = np.random.default_rng(SEED + 99)
+    lens = lens[:n_seqs]
+    tables = tables[:n_seqs]
+    nblk = (lens + BS - 1) // BS
+    used = np.concatenate([tables[b, : nblk[b]] for b in range(n_seqs)])
+    remap = {int(x): i for i, x in enumerate(used)}
+    t2 = np.full_like(tables, -1)
+    for b in range(n_seqs):
+        t2[b, : nblk[b]] = [remap[int(x)] for x in tables[b, : nblk[b]]]
+    kp = oracle.round_bf16(rng.standard_normal((used.size, hkv, BS, D)).astype(np.float32))
+    vp = oracle.round_bf16(rng.standard_normal((used.size, hkv, BS, D)).astype(np.float32))
+    q = oracle.round_bf16(rng.standard_normal((n_seqs, h, D)).astype(np.float32))
+    return q, kp, vp, t2, lens
+
+
+def cpu_baseline_single(lens, tables):
+    """The oracle port, single-threaded like the reference CpuAttention, on a sample of
+    the C2 step (the first 16 of 64 sequences, all heads); scaled to tokens/s."""
+    from oracle import oracle
+    n = 16
+    q, kp, vp, t2, l2 = _oracle_inputs(lens, tables, HKV, H, n)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.paged_decode(q, kp, vp, t2, l2, H, HKV, D, BS, kp.shape[0], num_threads=1)
+        reps += 1
+        if time.perf_counter() - t0 > 10.0:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(n / dt, 2), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n} of the 64 C2 sequences (all 32 heads, contexts as in the GPU run), "
+                      f"{reps} repetitions, {dt:.2f} s each; oracle/zl_oracle.c single thread"}
+
+
+def run_reference(args, rank, world):
+    """The reference CPU attention (oracle port) on all host cores, same metric/config."""
+    if rank != 0:
+        return
+    from oracle import oracle
+    cores = os.cpu_count() or 1
+    lens, tables, _ = make_lens_tables(world)
+    B = len(lens)
+    hkv, h = HKV, H  # the whole job's heads: the CPU does every shard's work
+    n = min(B, 64)
+    q, kp, vp, t2, l2 = _oracle_inputs(lens, tables, hkv, h, n)
+    for _ in range(args.warmup):
+        oracle.paged_decode(q, kp, vp, t2, l2, h, hkv, D, BS, kp.shape[0], num_threads=cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.paged_decode(q, kp, vp, t2, l2, h, hkv, D, BS, kp.shape[0], num_threads=cores)
+    dt = (time.perf_counter() - t0) / args.steps
+    val = n / dt
+    line = {"impl": "reference", "metric": "paged_decode_tokens_per_s", "value": round(val, 2),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) bf16-rounded q/K/V, U[512,4096] contexts)",
+            "config": {"workload": "C2 paged decode, Llama-3-8B layer shape (CPU reference path)",
+                       "global_batch": B, "sample_seqs_per_step": n, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                       "parallelism": f"{cores} host threads (OpenMP over (seq, head))"},
+            "cpu_baseline": {"value": round(val, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} sequences x 32 heads per step of the {B}-sequence job"},
+            "e2e": {"value": round(val, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-side", action="store_true", help="skip the prefill / cache side measurements")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    # torchrun sets WORLD_SIZE; a plain `python bench.py --gpus N` without it is one process.
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; running {world} rank(s)")
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,258 @@
+/*
+ * zealot_attn.h -- C ABI of libzealot_attn.so, the B200 (sm_100a) attention
+ * hot path of the Zealot inference engine.
+ *
+ * This is the FFI surface a Rust `CudaModelRunner` (src/cuda_runner.rs,
+ * src/gpu_context.rs, src/kv_cache.rs, src/attention/ of 0xnicholas/Zealot)
+ * binds with `extern "C"`. Every entry point names the reference interface it
+ * replaces as `path:line` inside that project.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only; device pointers are marked `device`;
+ *    the caller owns every device buffer (as the reference launchers never own
+ *    theirs, src/attention/cuda.rs:56-66,126-140). The library owns only the
+ *    opaque zl_ctx (split-KV workspace, tensor-map cache, NCCL communicator).
+ *  - Every launch takes an explicit stream (`zl_stream` = cudaStream_t; NULL
+ *    is the legacy default stream) and is asynchronous.
+ *  - One zl_ctx is driven from one host thread at a time, like the
+ *    reference GpuContext (src/gpu_context.rs:23-26).
+ *  - Errors: every call returns zl_status; zl_last_error() gives a
+ *    thread-local message. Kernels never trap: a bad block id or a timed-out
+ *    device wait sets a bit in the context's device status word and the kernel
+ *    skips the access; zl_check_status() synchronises the stream and reports it.
+ *  - There is no CPU fallback: without a CUDA device the calls return
+ *    ZL_ERR_CUDA.
+ */
+#ifndef ZEALOT_ATTN_H
+#define ZEALOT_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZL_ABI_VERSION 1
+
+/* Status codes. The ZL_ERR_* values from OUT_OF_BLOCKS on mirror the
+ * ZealotError variants of src/error.rs:4-47; a Rust wrapper maps the others
+ * to ZealotError::Internal(zl_last_error()). */
+typedef enum {
+  ZL_OK = 0,
+  ZL_ERR_INVALID_ARG = 1,        /* bad size / pointer / unsupported combination */
+  ZL_ERR_CUDA = 2,               /* a CUDA runtime call failed (message has the name) */
+  ZL_ERR_OOB_BLOCK = 3,          /* device: block id or slot outside the pool */
+  ZL_ERR_TIMEOUT = 4,            /* device: a bounded wait ran out */
+  ZL_ERR_NCCL = 5,               /* an NCCL call failed or NCCL is not loadable */
+  ZL_ERR_UNSUPPORTED = 6,        /* shape the build has no kernel for */
+  ZL_ERR_OUT_OF_BLOCKS = 7,      /* ZealotError::OutOfBlocks        (error.rs:11-12) */
+  ZL_ERR_STALE_HANDLE = 8,       /* ZealotError::StaleHandle        (error.rs:23-28) */
+  ZL_ERR_BLOCK_NOT_ALLOCATED = 9,/* ZealotError::BlockNotAllocated  (error.rs:8-9)   */
+  ZL_ERR_INVALID_BLOCK_SIZE = 10,/* ZealotError::InvalidBlockSize   (error.rs:14-15) */
+  ZL_ERR_INTERNAL = 11,          /* ZealotError::Internal           (error.rs:45-46) */
+  ZL_ERR_SEQUENCE_TOO_LONG = 12  /* ZealotError::SequenceTooLong    (error.rs:36-37) */
+} zl_status;
+
+typedef enum { ZL_F32 = 0, ZL_BF16 = 1 } zl_dtype;
+
+/* Query head -> KV head. GROUPED is the HF/Llama convention used by the
+ * reference CUDA kernel (paged_attention.cu:32); MODULO is the CPU runner's
+ * repeat_interleave_kv (model_runner_cpu.rs:295). Equal for MHA. */
+typedef enum { ZL_GQA_GROUPED = 0, ZL_GQA_MODULO = 1 } zl_gqa_map;
+
+typedef void* zl_stream;
+typedef struct zl_ctx zl_ctx;
+
+typedef struct {
+  int device;                 /* CUDA ordinal */
+  size_t workspace_bytes;     /* initial split-KV workspace; 0 = grow on demand */
+} zl_ctx_cfg;
+
+/* ----------------------------------------------------------------- context */
+
+/* Replaces GpuContext::new (src/gpu_context.rs:30-52): binds a device and
+ * creates the library state. cfg may be NULL (device 0). */
+zl_status zl_ctx_create(const zl_ctx_cfg* cfg, zl_ctx** out);
+zl_status zl_ctx_destroy(zl_ctx* ctx);
+/* Thread-local text of the last error returned on this thread. */
+const char* zl_last_error(void);
+const char* zl_status_string(zl_status s);
+int zl_abi_version(void);
+/* Synchronises `stream`, reads and clears the device status word, returns the
+ * first device-side error (ZL_ERR_OOB_BLOCK / ZL_ERR_TIMEOUT) or ZL_OK. */
+zl_status zl_check_status(zl_ctx* ctx, zl_stream stream);
+/* Number of kernels this context has launched (for launch accounting). */
+uint64_t zl_launch_count(const zl_ctx* ctx);
+
+/* ------------------------------------------------------- reshape_and_cache */
+
+/* Replaces KVCache::store_kv / append_kv (src/kv_cache.rs:212-357), which
+ * issued 2*T*Hkv device-to-device copies, with one kernel. Token t of
+ * k/v [T][Hkv][d] goes to slot s = slot_mapping[t] of the pools
+ * [num_blocks][Hkv][block_size][d] at element offset
+ *   (s / bs)*bs*Hkv*d + h*bs*d + (s % bs)*d          (kv_cache.rs:245-247).
+ * slot < 0 skips the token; slot >= num_blocks*bs sets ZL_ERR_OOB_BLOCK in
+ * the status word and skips it. Bit-exact byte copy. */
+zl_status zl_reshape_and_cache(zl_ctx* ctx, const void* k /*device*/, const void* v /*device*/,
+                               void* k_pool /*device*/, void* v_pool /*device*/,
+                               const int64_t* slot_mapping /*device*/, int64_t num_tokens,
+                               int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                               zl_dtype dtype, zl_stream stream);
+
+/* ------------------------------------------------------------ paged decode */
+
+/* Replaces CudaAttention::paged_forward (src/attention/cuda.rs:126-210) and
+ * its kernels paged_attention_kernel / paged_attention_gqa_kernel
+ * (paged_attention.cu:13-291): same argument set (q/out [B][H][d], pools
+ * [num_blocks][Hkv][bs][d], block_tables [B][max_blocks_per_seq] int32 with
+ * negative entries ending a sequence, seq_lens [B]) plus the pool size for
+ * bounds checks, the softmax scale (<= 0 means 1/sqrt(d)), the head mapping
+ * and the split-KV count (0 = automatic). q, pools and out share `dtype`.
+ * An empty context writes zeros. */
+zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const void* v_pool,
+                          const int32_t* block_tables, const int32_t* seq_lens, void* out,
+                          int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                          int block_size, int max_blocks_per_seq, int64_t num_blocks, float scale,
+                          zl_gqa_map gqa_map, int num_splits, zl_dtype dtype, zl_stream stream);
+
+/* Sequence-split form (one sequence's KV spread over GPUs): attends only to
+ * tokens [tok_begin[b], tok_end[b]) of each sequence (tok_begin may be NULL =
+ * 0) and writes the unnormalised partial triple per (b, h):
+ *   m [B][H] = max score, l [B][H] = sum e^(s-m), o [B][H][d] = sum e^(s-m) v,
+ * all fp32. Empty ranges give (-inf, 0, 0). No reference counterpart: the
+ * reference has no multi-GPU path; this is the north-star sequence split. */
+zl_status zl_paged_decode_partial(zl_ctx* ctx, const void* q, const void* k_pool,
+                                  const void* v_pool, const int32_t* block_tables,
+                                  const int32_t* tok_begin, const int32_t* tok_end, float* m,
+                                  float* l, float* o, int num_seqs, int num_heads,
+                                  int num_kv_heads, int head_dim, int block_size,
+                                  int max_blocks_per_seq, int64_t num_blocks, float scale,
+                                  zl_gqa_map gqa_map, zl_dtype dtype, zl_stream stream);
+
+/* Merges P partial triples: out[r] = sum_p e^(m_p - M) o_p / sum_p e^(m_p - M) l_p
+ * with m, l [P][rows], o [P][rows][d] fp32 and out [rows][d] in `dtype`. */
+zl_status zl_merge_partials(zl_ctx* ctx, const float* m, const float* l, const float* o,
+                            int num_parts, int64_t rows, int head_dim, void* out, zl_dtype dtype,
+                            zl_stream stream);
+
+/* ---------------------------------------------------------- varlen prefill */
+
+/* Replaces CudaAttention::forward_gpu (src/attention/cuda.rs:56-110) and
+ * tiled_attention_kernel (attention.cu:9-187). Packed varlen layout instead of
+ * one [H][L][d] sequence: q/out [T][H][d], k/v [T][Hkv][d], cu_seqlens
+ * [num_seqs+1] int32 (device), T = cu_seqlens[num_seqs]; max_seq_len bounds the
+ * launch. causal != 0 masks keys after the query. bf16 with head_dim 128 runs
+ * on the tcgen05/TMEM tensor-core kernel; other shapes on the CUDA-core kernel. */
+zl_status zl_prefill_varlen(zl_ctx* ctx, const void* q, const void* k, const void* v,
+                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len, void* out,
+                            int num_heads, int num_kv_heads, int head_dim, float scale, int causal,
+                            zl_gqa_map gqa_map, zl_dtype dtype, zl_stream stream);
+
+/* ----------------------------------------------------- multi-GPU (NCCL) */
+
+/* NCCL is loaded at run time (dlopen libnccl.so.2), so the library has no
+ * link-time NCCL dependency. No reference counterpart (the reference has no
+ * multi-GPU code); these carry the north-star sequence-split merge. */
+zl_status zl_nccl_get_unique_id(uint8_t id_out[128]);
+zl_status zl_nccl_init(zl_ctx* ctx, const uint8_t id[128], int nranks, int rank);
+/* All-gathers every rank's partial triple (m, l [rows], o [rows][d] fp32,
+ * device) into the context workspace and merges them into out [rows][d]. */
+zl_status zl_nccl_merge(zl_ctx* ctx, const float* m, const float* l, const float* o,
+                        int64_t rows, int head_dim, void* out, zl_dtype dtype, zl_stream stream);
+zl_status zl_nccl_finalize(zl_ctx* ctx);
+
+/* ------------------------------------------------------------ block manager */
+
+/* Restatement of BlockManager (src/block_manager.rs:41-165): LIFO free list
+ * (a fresh pool hands out ids 0,1,2,...), refcounts, per-block generation
+ * starting at 1; a handle whose generation differs is stale. Host only. */
+typedef struct zl_block_manager zl_block_manager;
+typedef struct {
+  uint64_t block_id;
+  uint64_t generation;
+} zl_block_handle; /* BlockHandle, block_manager.rs:18-24 */
+
+zl_status zl_block_manager_create(uint64_t num_gpu_blocks, uint64_t block_size,
+                                  zl_block_manager** out);          /* :88-104 */
+zl_status zl_block_manager_destroy(zl_block_manager* bm);
+zl_status zl_block_manager_try_allocate(zl_block_manager* bm, zl_block_handle* out); /* :108-122 */
+zl_status zl_block_manager_try_free(zl_block_manager* bm, const zl_block_handle* h); /* :125-135 */
+zl_status zl_block_manager_try_reference(zl_block_manager* bm, const zl_block_handle* h); /* :140-144 */
+uint64_t zl_block_manager_available(const zl_block_manager* bm);    /* :147-149 */
+
+/* --------------------------------------------------------------- KV cache */
+
+/* Restatement of KVCache (src/kv_cache.rs:51-357) for the device: per-layer
+ * K/V pools [num_blocks][Hkv][bs][d] (zero-filled), per-sequence device block
+ * tables of max_blocks int32 with -1 sentinels (:107-124), blocks from a
+ * BlockManager (:127-161). store_kv/append_kv build a slot mapping on the host
+ * and run one reshape_and_cache launch per layer call. */
+typedef struct zl_kv_cache zl_kv_cache;
+zl_status zl_kv_cache_create(zl_ctx* ctx, uint64_t num_blocks, int block_size, int num_layers,
+                             int num_kv_heads, int head_dim, zl_dtype dtype, zl_kv_cache** out);
+zl_status zl_kv_cache_destroy(zl_kv_cache* kv);
+zl_status zl_kv_cache_register_seq(zl_kv_cache* kv, const char* id, int max_blocks);   /* :107-124 */
+/* Returns the whole handle (the reference returns the id only and drops the
+ * handle, so its blocks could never be freed with a generation check). */
+zl_status zl_kv_cache_alloc_block(zl_kv_cache* kv, const char* id, zl_block_manager* bm,
+                                  zl_block_handle* handle_out);                       /* :127-161 */
+zl_status zl_kv_cache_release_seq(zl_kv_cache* kv, const char* id);                  /* :164-166 */
+zl_status zl_kv_cache_store_kv(zl_kv_cache* kv, int layer, const char* id, const void* k,
+                               const void* v, uint64_t start_token, uint64_t n_tokens,
+                               zl_stream stream);                                     /* :212-276 */
+zl_status zl_kv_cache_append_kv(zl_kv_cache* kv, int layer, const char* id, const void* k,
+                                const void* v, zl_stream stream);                     /* :281-357 */
+zl_status zl_kv_cache_cached_tokens(const zl_kv_cache* kv, const char* id, uint64_t* out);
+const int32_t* zl_kv_cache_block_table_ptr(const zl_kv_cache* kv, const char* id);    /* :191-194 */
+void* zl_kv_cache_k_pool_ptr(const zl_kv_cache* kv, int layer);                       /* :197-199 */
+void* zl_kv_cache_v_pool_ptr(const zl_kv_cache* kv, int layer);                       /* :202-204 */
+
+/* ------------------------------------------------------------ model runner */
+
+/* CudaModelRunner (src/cuda_runner.rs:271-658) with the math of the CPU
+ * runner it replaces (src/model_runner_cpu.rs:172-276): layer-0 weights,
+ * [in,out] row-major fp32, embedding -> q/k/v -> paged KV cache ->
+ * attention -> last row -> o-proj -> lm_head -> logits. Unlike the CPU runner
+ * it keeps a paged KV cache, so a decode step attends over the whole history
+ * (the CPU runner's recompute form). */
+typedef struct zl_runner zl_runner;
+typedef struct {
+  int hidden_dim, num_heads, num_kv_heads, head_dim, num_layers, vocab_size;
+  uint64_t num_gpu_blocks; /* SchedulerConfig::default: 1024 (scheduler.rs:168-178) */
+  int block_size;          /* 16 */
+  int max_blocks_per_seq;
+  zl_gqa_map gqa_map;      /* ZL_GQA_MODULO reproduces the CPU runner */
+} zl_runner_cfg;
+
+typedef struct {
+  const float* embedding; /* [vocab][hidden] */
+  const float* q_proj;    /* [hidden][H*d]   */
+  const float* k_proj;    /* [hidden][Hkv*d] */
+  const float* v_proj;    /* [hidden][Hkv*d] */
+  const float* attn_proj; /* [hidden][hidden]*/
+  const float* lm_head;   /* [hidden][vocab] */
+} zl_runner_weights;      /* host pointers, copied at create */
+
+/* One batch entry: what Sequence::step_input / is_prefill / prefill_pos
+ * (src/scheduler.rs:88-113) give the runner. */
+typedef struct {
+  const char* request_id;
+  const int64_t* tokens; /* host */
+  int num_tokens;
+  int is_prefill;
+  int prefill_pos;
+} zl_seq_input;
+
+zl_status zl_runner_create(zl_ctx* ctx, const zl_runner_cfg* cfg, const zl_runner_weights* w,
+                           zl_runner** out);                                  /* cuda_runner.rs:52-124 */
+zl_status zl_runner_destroy(zl_runner* r);
+/* ModelRunner::step (src/engine.rs:18): logits_out is host [n][vocab]. */
+zl_status zl_runner_step(zl_runner* r, const zl_seq_input* batch, int n, float* logits_out);
+/* ModelRunner::drop_state (src/engine.rs:22). Unknown ids are ignored. */
+zl_status zl_runner_drop_state(zl_runner* r, const char* request_id);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

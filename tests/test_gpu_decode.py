@@ -1,0 +1,182 @@
+"""Paged decode on the GPU against the CPU oracle (src/attention/mod.rs:64-97 row math
+over the block-table gather of paged_attention.cu). bf16: <= 2e-2 absolute after
+softmax, oracle fed the bf16-rounded inputs; fp32: <= 1e-4 relative."""
+import numpy as np
+import pytest
+
+from helpers import bf16_tensor, decode_case, f32_tensor, rel_err, to_f32
+
+pytestmark = pytest.mark.gpu
+
+BF16_ATOL = 2e-2
+F32_RTOL = 1e-4
+
+
+def _run_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs, gqa_map=0):
+    import torch
+    import zealot_b200 as zb
+    attn = zb.CudaAttention(ctx)
+    tq, q32 = bf16_tensor(oracle, q)
+    tk, k32 = bf16_tensor(oracle, kp)
+    tv, v32 = bf16_tensor(oracle, vp)
+    tt = torch.from_numpy(table).cuda()
+    tl = torch.from_numpy(np.asarray(lens, np.int32)).cuda()
+    out = torch.full_like(tq, float("nan"))
+    B = table.shape[0]
+    attn.paged_forward(tq, tk, tv, tt, tl, out, B, H, Hkv, d, bs, table.shape[1],
+                       num_blocks=kp.shape[0], gqa_map=gqa_map)
+    ctx.check_status()
+    ref = oracle.paged_decode(q32, k32, v32, table, lens, H, Hkv, d, bs, kp.shape[0],
+                              gqa_map=gqa_map, num_threads=8)
+    return to_f32(out), ref
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+def test_bf16_fast_path_small(ctx, oracle, G):
+    rng = np.random.default_rng(100 + G)
+    Hkv, d, bs = 2, 128, 16
+    H = Hkv * G
+    lens = [1, 15, 16, 17, 33, 100, 257, 511]
+    q, kp, vp, table, lens = decode_case(rng, len(lens), lens, H, Hkv, d, bs, 512)
+    got, ref = _run_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs)
+    assert np.max(np.abs(got - ref)) <= BF16_ATOL
+
+
+def test_bf16_empty_and_sentinel(ctx, oracle):
+    rng = np.random.default_rng(5)
+    H, Hkv, d, bs = 8, 2, 128, 16
+    lens = [0, 40, 200, 64]
+    q, kp, vp, table, lens = decode_case(rng, 4, lens, H, Hkv, d, bs, 256)
+    table[2, 5] = -1  # ends sequence 2 after 80 tokens (paged_attention.cu:66-67)
+    got, ref = _run_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs)
+    assert np.all(got[0] == 0)
+    assert np.max(np.abs(got - ref)) <= BF16_ATOL
+
+
+def test_bf16_long_context_split(ctx, oracle):
+    """Sequences far longer than one warp's share: the stream-K split and the
+    last-arriver merge run for almost every (sequence, kv head)."""
+    rng = np.random.default_rng(6)
+    H, Hkv, d, bs = 32, 8, 128, 16
+    lens = [60000, 3000, 17, 20001]
+    q, kp, vp, table, lens = decode_case(rng, 4, lens, H, Hkv, d, bs, 6000)
+    for _ in range(2):  # twice: the workspace counters must come back to zero
+        got, ref = _run_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs)
+        assert np.max(np.abs(got - ref)) <= BF16_ATOL
+
+
+def test_bf16_c2_full(ctx, oracle):
+    """Config C2 at full size: B=64, 32/8 heads, d=128, ctx U[512, 4096], block tables a
+    seeded random permutation of a 65536-block pool. The pools are drawn on the GPU; the
+    oracle gets the referenced blocks only, with the tables renumbered."""
+    import torch
+    import zealot_b200 as zb
+    rng = np.random.default_rng(2024)
+    B, H, Hkv, d, bs, nb = 64, 32, 8, 128, 16, 65536
+    lens = rng.integers(512, 4097, size=B).astype(np.int32)
+    nblk = (lens + bs - 1) // bs
+    perm = rng.permutation(nb).astype(np.int32)
+    table = np.full((B, 256), -1, np.int32)
+    off = 0
+    for b in range(B):
+        table[b, : nblk[b]] = perm[off: off + nblk[b]]
+        off += nblk[b]
+    g = torch.Generator(device="cuda").manual_seed(2024)
+    tk = torch.randn((nb, Hkv, bs, d), generator=g, device="cuda").to(torch.bfloat16)
+    tv = torch.randn((nb, Hkv, bs, d), generator=g, device="cuda").to(torch.bfloat16)
+    tq, q32 = bf16_tensor(oracle, rng.standard_normal((B, H, d)).astype(np.float32))
+    out = torch.empty_like(tq)
+    attn = zb.CudaAttention(ctx)
+    attn.paged_forward(tq, tk, tv, torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(),
+                       out, B, H, Hkv, d, bs, 256, num_blocks=nb)
+    ctx.check_status()
+    used = perm[:off]
+    idx = torch.from_numpy(used.astype(np.int64)).cuda()
+    k32 = tk.index_select(0, idx).float().cpu().numpy()
+    v32 = tv.index_select(0, idx).float().cpu().numpy()
+    remap = np.full(nb, -1, np.int64)
+    remap[used] = np.arange(used.size)
+    t2 = np.where(table >= 0, remap[np.maximum(table, 0)], -1).astype(np.int32)
+    ref = oracle.paged_decode(q32, k32, v32, t2, lens, H, Hkv, d, bs, used.size, num_threads=8)
+    assert np.max(np.abs(to_f32(out) - ref)) <= BF16_ATOL
+
+
+def test_bf16_modulo_mapping(ctx, oracle):
+    rng = np.random.default_rng(8)
+    H, Hkv, d, bs = 8, 2, 128, 16
+    q, kp, vp, table, lens = decode_case(rng, 3, [30, 99, 160], H, Hkv, d, bs, 64)
+    got, ref = _run_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs, gqa_map=1)
+    assert np.max(np.abs(got - ref)) <= BF16_ATOL
+
+
+@pytest.mark.parametrize("shape", [(4, 4, 8, 16), (8, 2, 64, 16), (4, 1, 32, 8)])
+def test_f32_generic(ctx, oracle, shape):
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d, bs = shape
+    rng = np.random.default_rng(sum(shape))
+    q, kp, vp, table, lens = decode_case(rng, 5, [1, 7, 64, 65, 300], H, Hkv, d, bs, 128)
+    attn = zb.CudaAttention(ctx)
+    out = torch.empty(q.shape, dtype=torch.float32, device="cuda")
+    attn.paged_forward(f32_tensor(q), f32_tensor(kp), f32_tensor(vp), torch.from_numpy(table).cuda(),
+                       torch.from_numpy(lens).cuda(), out, 5, H, Hkv, d, bs, table.shape[1])
+    ctx.check_status()
+    ref = oracle.paged_decode(q, kp, vp, table, lens, H, Hkv, d, bs, kp.shape[0])
+    for b in range(5):
+        assert rel_err(out[b].cpu().numpy(), ref[b]) <= F32_RTOL
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_oob_block_id_is_reported(ctx, oracle, dtype):
+    import torch
+    import zealot_b200 as zb
+    rng = np.random.default_rng(9)
+    H, Hkv, d, bs = 4, 2, 128, 16
+    q, kp, vp, table, lens = decode_case(rng, 2, [40, 40], H, Hkv, d, bs, 32)
+    table[1, 1] = 32  # == num_blocks
+    with pytest.raises(oracle.OracleError):
+        oracle.paged_decode(q, kp, vp, table, lens, H, Hkv, d, bs, 32)
+    attn = zb.CudaAttention(ctx)
+    if dtype == "bf16":
+        tq, tk, tv = (bf16_tensor(oracle, x)[0] for x in (q, kp, vp))
+    else:
+        tq, tk, tv = f32_tensor(q), f32_tensor(kp), f32_tensor(vp)
+    out = torch.empty_like(tq)
+    attn.paged_forward(tq, tk, tv, torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(), out,
+                       2, H, Hkv, d, bs, table.shape[1], num_blocks=32)
+    with pytest.raises(zb.OobBlockError):
+        ctx.check_status()
+    ctx.check_status()  # the status word was cleared by the first read
+
+
+def test_partial_and_merge(ctx, oracle):
+    """Sequence split: partial triples over two token ranges merge to the full decode."""
+    import torch
+    import zealot_b200 as zb
+    rng = np.random.default_rng(10)
+    B, H, Hkv, d, bs = 4, 8, 2, 128, 16
+    q, kp, vp, table, lens = decode_case(rng, B, [50, 300, 16, 1000], H, Hkv, d, bs, 256)
+    attn = zb.CudaAttention(ctx)
+    tq, q32 = bf16_tensor(oracle, q)
+    tk, k32 = bf16_tensor(oracle, kp)
+    tv, v32 = bf16_tensor(oracle, vp)
+    tt = torch.from_numpy(table).cuda()
+    cut = np.array([20, 150, 0, 999], np.int32)
+    zeros = np.zeros(B, np.int32)
+    ms, ls, os_ = [], [], []
+    for lo, hi in ((zeros, cut), (cut, lens)):
+        m = torch.empty((B, H), dtype=torch.float32, device="cuda")
+        l = torch.empty_like(m)
+        o = torch.empty((B, H, d), dtype=torch.float32, device="cuda")
+        attn.paged_forward_partial(tq, tk, tv, tt, torch.from_numpy(lo).cuda(), torch.from_numpy(hi).cuda(),
+                                   m, l, o, B, H, Hkv, d, bs, table.shape[1])
+        rm, rl, ro = oracle.paged_decode_partial(q32, k32, v32, table, lo, hi, H, Hkv, d, bs, kp.shape[0])
+        np.testing.assert_allclose(m.cpu().numpy(), rm, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(l.cpu().numpy(), rl, rtol=1e-4)
+        np.testing.assert_allclose(o.cpu().numpy(), ro, rtol=1e-4, atol=1e-3)
+        ms.append(m); ls.append(l); os_.append(o)
+    out = torch.empty((B, H, d), dtype=torch.float32, device="cuda")
+    attn.merge_partials(torch.stack(ms), torch.stack(ls), torch.stack(os_), out)
+    ctx.check_status()
+    full = oracle.paged_decode(q32, k32, v32, table, lens, H, Hkv, d, bs, kp.shape[0])
+    assert rel_err(out.cpu().numpy(), full) <= 1e-4

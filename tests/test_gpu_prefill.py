@@ -1,0 +1,86 @@
+"""Varlen prefill on the GPU against the oracle's causal rows (each row is the
+CpuAttention last row on its prefix, src/attention/mod.rs:64-97)."""
+import numpy as np
+import pytest
+
+from helpers import bf16_tensor, f32_tensor, rel_err, to_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(rng, lens, H, Hkv, d):
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    q = rng.standard_normal((T, H, d)).astype(np.float32)
+    k = rng.standard_normal((T, Hkv, d)).astype(np.float32)
+    v = rng.standard_normal((T, Hkv, d)).astype(np.float32)
+    return cu, q, k, v
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("shape", [(4, 4, 8), (8, 2, 64), (4, 1, 128)])
+def test_f32_prefill(ctx, oracle, shape, causal):
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = shape
+    rng = np.random.default_rng(d + H)
+    lens = [1, 37, 128, 200]
+    cu, q, k, v = _case(rng, lens, H, Hkv, d)
+    out = torch.empty(q.shape, dtype=torch.float32, device="cuda")
+    zb.CudaAttention(ctx).forward_gpu(f32_tensor(q), f32_tensor(k), f32_tensor(v),
+                                      torch.from_numpy(cu).cuda(), out, H, Hkv, d, max(lens),
+                                      causal=causal)
+    ctx.check_status()
+    ref = oracle.prefill_varlen(q, k, v, cu, H, Hkv, d, causal=causal, num_threads=8)
+    got = out.cpu().numpy()
+    for r in range(q.shape[0]):
+        assert rel_err(got[r], ref[r]) <= 1e-4
+
+
+@pytest.mark.parametrize("lens", [[1, 127, 128, 129], [300, 700, 5, 1024], [2000]])
+def test_bf16_prefill_d128(ctx, oracle, lens):
+    """bf16, head_dim 128, GQA 32/8: the tensor-core path (tcgen05) when it applies."""
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = 32, 8, 128
+    rng = np.random.default_rng(sum(lens))
+    cu, q, k, v = _case(rng, lens, H, Hkv, d)
+    tq, q32 = bf16_tensor(oracle, q)
+    tk, k32 = bf16_tensor(oracle, k)
+    tv, v32 = bf16_tensor(oracle, v)
+    out = torch.full_like(tq, float("nan"))
+    zb.CudaAttention(ctx).forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d,
+                                      max(lens), causal=True)
+    ctx.check_status()
+    ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=True, num_threads=8)
+    assert np.max(np.abs(to_f32(out) - ref)) <= 2e-2
+
+
+def test_bf16_prefill_c3_sampled(ctx, oracle):
+    """Config C3 shape (16 sequences, L U[256, 8192], 32/8 heads, d 128): full GPU run,
+    oracle on a seeded sample of rows (first, last, block edges, random)."""
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = 32, 8, 128
+    rng = np.random.default_rng(3)
+    lens = rng.integers(256, 8193, size=16)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    g = torch.Generator(device="cuda").manual_seed(3)
+    tq = torch.randn((T, H, d), generator=g, device="cuda").to(torch.bfloat16)
+    tk = torch.randn((T, Hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    tv = torch.randn((T, Hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(tq)
+    zb.CudaAttention(ctx).forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d,
+                                      int(lens.max()), causal=True)
+    ctx.check_status()
+    rows = set()
+    for s in range(16):
+        for i in (0, 1, 127, 128, int(lens[s]) - 1):
+            rows.add(int(cu[s]) + min(i, int(lens[s]) - 1))
+    rows |= set(int(x) for x in rng.integers(0, T, size=48))
+    rows = np.array(sorted(rows), np.int64)
+    q32, k32, v32 = (t.float().cpu().numpy() for t in (tq, tk, tv))
+    ref = oracle.prefill_varlen_rows(q32, k32, v32, cu, rows, H, Hkv, d, causal=True, num_threads=8)
+    got = out.float().cpu().numpy()[rows]
+    assert np.max(np.abs(got - ref)) <= 2e-2

@@ -1,0 +1,115 @@
+"""ctypes binding of include/zealot_attn.h (libzealot_attn.so).
+
+This is the Python twin of the `extern "C"` block a Rust host would write
+(see INTEGRATION.md). It loads the in-tree library and declares every entry
+point; nothing here computes.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzealot_attn.so")
+
+c_int, c_int64, c_uint64, c_float, c_size_t = (ctypes.c_int, ctypes.c_int64, ctypes.c_uint64,
+                                               ctypes.c_float, ctypes.c_size_t)
+c_void_p, c_char_p = ctypes.c_void_p, ctypes.c_char_p
+P = ctypes.POINTER
+
+
+class zl_ctx_cfg(ctypes.Structure):
+    _fields_ = [("device", c_int), ("workspace_bytes", c_size_t)]
+
+
+class zl_block_handle(ctypes.Structure):
+    _fields_ = [("block_id", c_uint64), ("generation", c_uint64)]
+
+
+class zl_runner_cfg(ctypes.Structure):
+    _fields_ = [("hidden_dim", c_int), ("num_heads", c_int), ("num_kv_heads", c_int),
+                ("head_dim", c_int), ("num_layers", c_int), ("vocab_size", c_int),
+                ("num_gpu_blocks", c_uint64), ("block_size", c_int),
+                ("max_blocks_per_seq", c_int), ("gqa_map", c_int)]
+
+
+class zl_runner_weights(ctypes.Structure):
+    _fields_ = [(n, P(c_float)) for n in ("embedding", "q_proj", "k_proj", "v_proj",
+                                          "attn_proj", "lm_head")]
+
+
+class zl_seq_input(ctypes.Structure):
+    _fields_ = [("request_id", c_char_p), ("tokens", P(c_int64)), ("num_tokens", c_int),
+                ("is_prefill", c_int), ("prefill_pos", c_int)]
+
+
+# name -> (restype, argtypes); every symbol declared in include/zealot_attn.h
+SIGNATURES = {
+    "zl_ctx_create": (c_int, [P(zl_ctx_cfg), P(c_void_p)]),
+    "zl_ctx_destroy": (c_int, [c_void_p]),
+    "zl_last_error": (c_char_p, []),
+    "zl_status_string": (c_char_p, [c_int]),
+    "zl_abi_version": (c_int, []),
+    "zl_check_status": (c_int, [c_void_p, c_void_p]),
+    "zl_launch_count": (c_uint64, [c_void_p]),
+    "zl_reshape_and_cache": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_int64, c_int, c_int, c_int, c_int64, c_int, c_void_p]),
+    "zl_paged_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int64,
+                                c_float, c_int, c_int, c_int, c_void_p]),
+    "zl_paged_decode_partial": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                        c_int, c_int, c_int, c_int, c_int, c_int64, c_float, c_int,
+                                        c_int, c_void_p]),
+    "zl_merge_partials": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int,
+                                  c_void_p, c_int, c_void_p]),
+    "zl_prefill_varlen": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                  c_void_p, c_int, c_int, c_int, c_float, c_int, c_int, c_int,
+                                  c_void_p]),
+    "zl_nccl_get_unique_id": (c_int, [c_void_p]),
+    "zl_nccl_init": (c_int, [c_void_p, c_void_p, c_int, c_int]),
+    "zl_nccl_merge": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+                              c_int, c_void_p]),
+    "zl_nccl_finalize": (c_int, [c_void_p]),
+    "zl_block_manager_create": (c_int, [c_uint64, c_uint64, P(c_void_p)]),
+    "zl_block_manager_destroy": (c_int, [c_void_p]),
+    "zl_block_manager_try_allocate": (c_int, [c_void_p, P(zl_block_handle)]),
+    "zl_block_manager_try_free": (c_int, [c_void_p, P(zl_block_handle)]),
+    "zl_block_manager_try_reference": (c_int, [c_void_p, P(zl_block_handle)]),
+    "zl_block_manager_available": (c_uint64, [c_void_p]),
+    "zl_kv_cache_create": (c_int, [c_void_p, c_uint64, c_int, c_int, c_int, c_int, c_int,
+                                   P(c_void_p)]),
+    "zl_kv_cache_destroy": (c_int, [c_void_p]),
+    "zl_kv_cache_register_seq": (c_int, [c_void_p, c_char_p, c_int]),
+    "zl_kv_cache_alloc_block": (c_int, [c_void_p, c_char_p, c_void_p, P(zl_block_handle)]),
+    "zl_kv_cache_release_seq": (c_int, [c_void_p, c_char_p]),
+    "zl_kv_cache_store_kv": (c_int, [c_void_p, c_int, c_char_p, c_void_p, c_void_p, c_uint64,
+                                     c_uint64, c_void_p]),
+    "zl_kv_cache_append_kv": (c_int, [c_void_p, c_int, c_char_p, c_void_p, c_void_p, c_void_p]),
+    "zl_kv_cache_cached_tokens": (c_int, [c_void_p, c_char_p, P(c_uint64)]),
+    "zl_kv_cache_block_table_ptr": (c_void_p, [c_void_p, c_char_p]),
+    "zl_kv_cache_k_pool_ptr": (c_void_p, [c_void_p, c_int]),
+    "zl_kv_cache_v_pool_ptr": (c_void_p, [c_void_p, c_int]),
+    "zl_runner_create": (c_int, [c_void_p, P(zl_runner_cfg), P(zl_runner_weights), P(c_void_p)]),
+    "zl_runner_destroy": (c_int, [c_void_p]),
+    "zl_runner_step": (c_int, [c_void_p, P(zl_seq_input), c_int, P(c_float)]),
+    "zl_runner_drop_state": (c_int, [c_void_p, c_char_p]),
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Loads libzealot_attn.so and declares its signatures. Raises if the
+    library has not been built: there is no Python fallback."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise ImportError(f"{path} is missing: build it with `python -m zealot_b200.build`")
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib

@@ -1,0 +1,557 @@
+// paged_decode_bf16.cu -- HBM-bound paged decode attention for bf16 pools,
+// head_dim 128, block_size 16, GQA groups of up to 8 query heads.
+//
+// Replaces paged_attention_kernel / paged_attention_gqa_kernel
+// (src/attention/kernels/paged_attention.cu:13-291 of the reference), where
+// thread 0 of a CTA did all the math over scalar loads.
+//
+// Design (B200):
+//  * Work is the flat list of (sequence, kv head, 16-token block) triples in
+//    (b, kvh, j) order. A persistent grid (one CTA per SM, WARPS warps each)
+//    splits that list into equal contiguous ranges, one per warp ("stream-K"
+//    at block granularity), so ragged contexts cost no load imbalance.
+//  * Each warp runs its own STAGES-deep ring in shared memory: lane 0 issues
+//    TMA tile loads (two 64-column boxes per K and per V tile, 128-byte
+//    swizzle) that complete on an mbarrier, all lanes consume.
+//  * Math on the warp-level tensor-core path: S^T = K * q^T (m16n8k16, the 16
+//    tokens of a block are M, the <=8 heads of the group are N), online
+//    softmax in registers with warp shuffles, P^T re-laid out by movmatrix,
+//    O^T += V^T * P^T with ldmatrix.trans. Every loaded K/V tile serves the
+//    whole GQA group. fp32 accumulation.
+//  * A (sequence, kv head) that spans several warps is merged by the last
+//    warp to finish it (atomic counter in a self-resetting workspace), so
+//    there is no second kernel.
+#include "zl_internal.h"
+#include "zl_ptx.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace {
+
+using namespace zl::ptx;
+
+constexpr int D = 128;           // head dim
+constexpr int BS = 16;           // tokens per block
+constexpr int TILE = BS * D * 2; // bytes of one K (or V) block tile = 4 KB
+constexpr int STAGE = 2 * TILE;  // K + V
+constexpr int MAX_G = 8;         // query heads per kv head handled per pass
+constexpr int MAX_B = 4096;      // sequences per launch (prefix table in smem)
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+// Per-warp partial triple in the workspace.
+struct Partial {
+  float m[MAX_G];
+  float l[MAX_G];
+  float o[MAX_G][D];
+};
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;      // [B][H][D]
+  const int32_t* block_tables; // [B][max_blocks]
+  const int32_t* seq_lens;     // [B]
+  __nv_bfloat16* out;          // [B][H][D]
+  Partial* partials;           // [2*W]
+  int* counters;               // [B*Hkv], zero on entry, zero on exit
+  int* status;
+  int B, H, Hkv, G, max_blocks;
+  int64_t num_blocks;
+  float scale_log2;            // scale * log2(e)
+};
+
+template <int WARPS, int STAGES>
+struct Smem {
+  static constexpr int kRing = WARPS * STAGES * STAGE;
+  static constexpr int kBars = WARPS * STAGES * 8;
+  static constexpr int kInfo = WARPS * STAGES * 4;
+  static constexpr int kPrefix = (MAX_B + 1) * 4;
+  static constexpr int kTotal = 1024 /*alignment slack*/ + kRing + kBars + kInfo + kPrefix + 16;
+};
+
+// Swizzled byte offset of (row r, 16-byte chunk c in 0..15) inside a K or V
+// tile: two 2 KB boxes of [16 rows][64 cols], 128-byte swizzle (chunk ^= row%8).
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {
+  return (uint32_t)((c >> 3) * 2048 + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
+}
+
+// Warp index owning flat block x when TB blocks are split over W warps as
+// [gw*TB/W, (gw+1)*TB/W).
+__device__ __forceinline__ int owner_warp(int64_t x, int64_t TB, int64_t W) {
+  return (int)(((x + 1) * W - 1) / TB);
+}
+
+template <int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV) {
+  using SM = Smem<WARPS, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u32 - raw_u32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + SM::kRing);
+  int* info = reinterpret_cast<int*>(base + SM::kRing + SM::kBars);
+  int* prefix = reinterpret_cast<int*>(base + SM::kRing + SM::kBars + SM::kInfo);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = a.B, Hkv = a.Hkv;
+
+  if (tid == 0) {
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  for (int i = tid; i < WARPS * STAGES; i += blockDim.x) mbar_init(smem_u32(&bars[i]), 1);
+
+  // ---- per-CTA prologue: prefix[b] = Hkv * sum_{b'<b} nblk(b') (flat start of b)
+  {
+    constexpr int T = WARPS * 32;
+    const int per = (B + T - 1) / T;
+    const int b0 = tid * per;
+    int local = 0;
+    for (int k = 0; k < per; k++) {
+      const int b = b0 + k;
+      if (b < B) {
+        const int len = max(a.seq_lens[b], 0);
+        int nb = (len + BS - 1) / BS;
+        if (nb > a.max_blocks) {
+          if (blockIdx.x == 0) atomicOr(a.status, ZL_DEV_OOB);
+          nb = a.max_blocks;
+        }
+        local += nb;
+      }
+    }
+    // block-wide exclusive scan of `local`
+    int incl = local;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    __shared__ int warp_tot[WARPS];
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int run = incl - local;
+    for (int w = 0; w < warp; w++) run += warp_tot[w];
+    if (tid == 0) prefix[0] = 0;
+    for (int k = 0; k < per; k++) {
+      const int b = b0 + k;
+      if (b < B) {
+        const int len = max(a.seq_lens[b], 0);
+        run += min((len + BS - 1) / BS, a.max_blocks);
+        prefix[b + 1] = run;
+      }
+    }
+  }
+  fence_mbar_init();
+  __syncthreads();
+
+  const int64_t NB = prefix[B];         // sum of blocks over sequences
+  const int64_t TB = NB * Hkv;          // flat work items
+  const int64_t W = (int64_t)gridDim.x * WARPS;
+  const int gw = blockIdx.x * WARPS + warp;
+
+  // Sequences with no context produce zeros (CTA 0 writes them).
+  if (blockIdx.x == 0) {
+    for (int b = warp; b < B; b += WARPS) {
+      if (prefix[b + 1] == prefix[b]) {
+        uint2 z = make_uint2(0, 0);
+        for (int i = lane; i < a.H * D / 4; i += 32)
+          reinterpret_cast<uint2*>(a.out + (int64_t)b * a.H * D)[i] = z;
+      }
+    }
+  }
+  if (TB == 0) return;
+
+  const int64_t f0 = (int64_t)gw * TB / W;
+  const int64_t f1 = (int64_t)(gw + 1) * TB / W;
+  const int nwork = (int)(f1 - f0);
+  if (nwork <= 0) return;
+
+  // Locate flat index f0: sequence b (largest with Hkv*prefix[b] <= f0).
+  auto locate = [&](int64_t f, int& b, int& kvh, int& j) {
+    int lo = 0, hi = B;  // Hkv*prefix[lo] <= f < Hkv*prefix[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if ((int64_t)prefix[mid] * Hkv <= f) lo = mid; else hi = mid;
+    }
+    // skip empty sequences (prefix equal)
+    while ((int64_t)prefix[lo + 1] * Hkv <= f) lo++;
+    b = lo;
+    const int nb = prefix[b + 1] - prefix[b];
+    const int64_t off = f - (int64_t)prefix[b] * Hkv;
+    kvh = (int)(off / nb);
+    j = (int)(off - (int64_t)kvh * nb);
+  };
+
+  const uint32_t ring = base_u32 + warp * STAGES * STAGE;
+  uint64_t* wbars = bars + warp * STAGES;
+  int* winfo = info + warp * STAGES;
+  const uint64_t policy = policy_evict_first();
+
+  // ---------------- producer state (lane 0 only) ----------------
+  int pb = 0, pkvh = 0, pj = 0;
+  bool ptrunc = false;
+  {
+    int b, kvh, j;
+    locate(f0, b, kvh, j);
+    pb = b; pkvh = kvh; pj = j;
+    // A negative entry before j (in a block another warp handles) ends the
+    // sequence for this warp too.
+    bool neg = false;
+    const int32_t* tb = a.block_tables + (int64_t)b * a.max_blocks;
+    for (int t = lane; t < j; t += 32) neg |= (tb[t] < 0);
+    ptrunc = __any_sync(0xffffffffu, neg);
+  }
+  auto produce = [&](int i) {
+    // called by lane 0 for the i-th block of this warp's range
+    const int slot = i % STAGES;
+    const int nb = prefix[pb + 1] - prefix[pb];
+    if (pj == 0) ptrunc = false;
+    const int32_t e = a.block_tables[(int64_t)pb * a.max_blocks + pj];
+    int nvalid = 0;
+    if (!ptrunc) {
+      if (e < 0) {
+        ptrunc = true;
+      } else if ((int64_t)e >= a.num_blocks) {
+        atomicOr(a.status, ZL_DEV_OOB);
+      } else {
+        const int len = a.seq_lens[pb];
+        nvalid = (pj == nb - 1) ? (len - pj * BS) : BS;
+      }
+    }
+    winfo[slot] = nvalid;
+    const uint32_t bar = smem_u32(&wbars[slot]);
+    if (nvalid > 0) {
+      const uint32_t dst = ring + slot * STAGE;
+      const int y = (int)(((int64_t)e * Hkv + pkvh) * BS);
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(bar, STAGE);
+      tma_load_2d_hint(dst, &tmK, 0, y, bar, policy);
+      tma_load_2d_hint(dst + 2048, &tmK, 64, y, bar, policy);
+      tma_load_2d_hint(dst + TILE, &tmV, 0, y, bar, policy);
+      tma_load_2d_hint(dst + TILE + 2048, &tmV, 64, y, bar, policy);
+    } else {
+      mbar_arrive(bar);
+    }
+    // advance (b, kvh, j)
+    if (++pj == nb) {
+      pj = 0;
+      if (++pkvh == Hkv) {
+        pkvh = 0;
+        do { pb++; } while (pb < B && prefix[pb + 1] == prefix[pb]);
+      }
+    }
+  };
+
+  if (lane == 0) {
+    const int pre = min(nwork, STAGES);
+    for (int i = 0; i < pre; i++) produce(i);
+  }
+  __syncwarp();
+
+  // ---------------- consumer state (all lanes) ----------------
+  int cb, ckvh, cj;
+  locate(f0, cb, ckvh, cj);
+  const int quad = lane >> 2;   // 0..7 : token row (S), head column (B operand)
+  const int qid = lane & 3;     // 0..3
+  const int mat = lane >> 3, mrow = lane & 7;
+  bool timed_out = false;
+
+  int i = 0;
+  while (i < nwork && !timed_out) {
+    // ----- segment (cb, ckvh) starting at block cj
+    const int nb = prefix[cb + 1] - prefix[cb];
+    const int seg_j0 = cj;
+    const int64_t seg_S = (int64_t)prefix[cb] * Hkv + (int64_t)ckvh * nb;
+    const int64_t seg_E = seg_S + nb;
+    const int64_t seg_rem = f1 - seg_S;
+    const int seg_jend = seg_rem < (int64_t)nb ? (int)seg_rem : nb;  // exclusive
+    const int G = a.G;
+    const int head0 = ckvh * G;
+
+    // q fragments (B operand of S^T = K q^T): head n = quad, d pairs
+    uint32_t qf[8][2];
+    {
+      const bool hv = quad < G;
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+          a.q + ((int64_t)cb * a.H + head0 + (hv ? quad : 0)) * D);
+#pragma unroll
+      for (int ks = 0; ks < 8; ks++) {
+        qf[ks][0] = hv ? __ldg(qrow + ks * 8 + qid) : 0u;
+        qf[ks][1] = hv ? __ldg(qrow + ks * 8 + 4 + qid) : 0u;
+      }
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+
+    for (int j = seg_j0; j < seg_jend; j++, i++) {
+      const int slot = i % STAGES;
+      const uint32_t bar = smem_u32(&wbars[slot]);
+      if (!mbar_wait(bar, (uint32_t)((i / STAGES) & 1), a.status)) {
+        timed_out = true;
+        break;
+      }
+      const int nvalid = winfo[slot];
+      const uint32_t ks_base = ring + slot * STAGE;
+      const uint32_t vs_base = ks_base + TILE;
+      if (nvalid > 0) {
+        if (nvalid < BS) {
+          // zero V rows past the context so 0 * garbage cannot be NaN
+          uint8_t* vt = base + (vs_base - base_u32);
+          for (int x = lane; x < (BS - nvalid) * 16; x += 32) {
+            const int r = nvalid + (x >> 4), c = x & 15;
+            *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
+          }
+          __syncwarp();
+        }
+        // S^T[16 tok][8 heads] = K[16][128] * q^T
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+          uint32_t a0, a1, a2, a3;
+          const int r = mrow + ((mat & 1) << 3);
+          const int c = 2 * ks + (mat >> 1);
+          ldsm_x4(ks_base + tile_off(r, c), a0, a1, a2, a3);
+          mma_bf16_16816(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+        }
+        // mask + scale to log2 units
+        const bool v0 = quad < nvalid, v1 = quad + 8 < nvalid;
+        s[0] = v0 ? s[0] * a.scale_log2 : -INFINITY;
+        s[1] = v0 ? s[1] * a.scale_log2 : -INFINITY;
+        s[2] = v1 ? s[2] * a.scale_log2 : -INFINITY;
+        s[3] = v1 ? s[3] * a.scale_log2 : -INFINITY;
+        float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+          bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+        }
+        const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+        const float al0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mn0);
+        const float al1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mn1);
+        m0 = mn0; m1 = mn1;
+        const float p0 = ex2(s[0] - mn0), p1 = ex2(s[1] - mn1);
+        const float p2 = ex2(s[2] - mn0), p3 = ex2(s[3] - mn1);
+        l0 = l0 * al0 + (p0 + p2);
+        l1 = l1 * al1 + (p1 + p3);
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+          o[t][0] *= al0; o[t][1] *= al1; o[t][2] *= al0; o[t][3] *= al1;
+        }
+        // P^T as the B operand: transpose the two 8x8 (tok x head) halves
+        const uint32_t b0 = movm_t(pack_bf16x2(p0, p1));
+        const uint32_t b1 = movm_t(pack_bf16x2(p2, p3));
+        // O^T[128 d][8 heads] += V^T * P^T
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+          uint32_t a0, a1, a2, a3;
+          const int r = mrow + ((mat >> 1) << 3);
+          const int c = 2 * t + (mat & 1);
+          ldsm_x4_t(vs_base + tile_off(r, c), a0, a1, a2, a3);
+          mma_bf16_16816(o[t], a0, a1, a2, a3, b0, b1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && i + STAGES < nwork) produce(i + STAGES);
+      __syncwarp();
+    }
+    if (timed_out) break;
+
+    // ----- finish the segment
+    const int nb_cur = nb;
+    float L0 = l0, L1 = l1;
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      L0 += __shfl_xor_sync(0xffffffffu, L0, off);
+      L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+    }
+    const int n0 = 2 * qid, n1 = 2 * qid + 1;  // head columns of this lane
+    const bool whole = (seg_S >= f0) && (seg_E <= f1);
+    if (whole) {
+      const float i0 = L0 > 0.f ? 1.f / L0 : 0.f, i1 = L1 > 0.f ? 1.f / L1 : 0.f;
+      __nv_bfloat16* ob = a.out + ((int64_t)cb * a.H + head0) * D;
+#pragma unroll
+      for (int t = 0; t < 8; t++) {
+        const int d0 = 16 * t + quad;
+        if (n0 < G) {
+          ob[n0 * D + d0] = __float2bfloat16_rn(o[t][0] * i0);
+          ob[n0 * D + d0 + 8] = __float2bfloat16_rn(o[t][2] * i0);
+        }
+        if (n1 < G) {
+          ob[n1 * D + d0] = __float2bfloat16_rn(o[t][1] * i1);
+          ob[n1 * D + d0 + 8] = __float2bfloat16_rn(o[t][3] * i1);
+        }
+      }
+    } else {
+      const int e = (seg_S <= f0 && f0 < seg_E) ? 0 : 1;
+      Partial* pp = a.partials + 2 * gw + e;
+      if (quad == 0) {
+        if (n0 < G) { pp->m[n0] = m0 * LN2; pp->l[n0] = L0; }
+        if (n1 < G) { pp->m[n1] = m1 * LN2; pp->l[n1] = L1; }
+      }
+#pragma unroll
+      for (int t = 0; t < 8; t++) {
+        const int d0 = 16 * t + quad;
+        if (n0 < G) { pp->o[n0][d0] = o[t][0]; pp->o[n0][d0 + 8] = o[t][2]; }
+        if (n1 < G) { pp->o[n1][d0] = o[t][1]; pp->o[n1][d0 + 8] = o[t][3]; }
+      }
+      __threadfence();
+      __syncwarp();
+      const int cidx = cb * Hkv + ckvh;
+      const int wa = owner_warp(seg_S, TB, W), wb = owner_warp(seg_E - 1, TB, W);
+      const int ncontrib = wb - wa + 1;
+      int old = 0;
+      if (lane == 0) old = atomicAdd(&a.counters[cidx], 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == ncontrib - 1) {
+        __threadfence();
+        // merge all contributors of this (sequence, kv head)
+        for (int n = 0; n < G; n++) {
+          float M = -INFINITY;
+          for (int c = wa; c <= wb; c++) {
+            const int64_t fc = (int64_t)c * TB / W;
+            const int ec = (c == wa && fc < seg_S) ? 1 : 0;
+            M = fmaxf(M, __ldcg(&a.partials[2 * c + ec].m[n]));
+          }
+          float den = 0.f;
+          float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c = wa; c <= wb; c++) {
+            const int64_t fc = (int64_t)c * TB / W;
+            const int ec = (c == wa && fc < seg_S) ? 1 : 0;
+            const Partial* pc = a.partials + 2 * c + ec;
+            const float mc = __ldcg(&pc->m[n]);
+            if (mc == -INFINITY) continue;
+            const float w = __expf(mc - M);
+            den += w * __ldcg(&pc->l[n]);
+            const float4 oc = __ldcg(reinterpret_cast<const float4*>(&pc->o[n][0]) + lane);
+            num.x += w * oc.x; num.y += w * oc.y; num.z += w * oc.z; num.w += w * oc.w;
+          }
+          const float inv = den > 0.f ? 1.f / den : 0.f;
+          __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
+          __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
+          uint2 pk;
+          pk.x = *reinterpret_cast<uint32_t*>(&lo);
+          pk.y = *reinterpret_cast<uint32_t*>(&hi);
+          reinterpret_cast<uint2*>(a.out + ((int64_t)cb * a.H + head0 + n) * D)[lane] = pk;
+        }
+        if (lane == 0) a.counters[cidx] = 0;
+      }
+    }
+    (void)nb_cur;
+    // advance consumer to the next segment
+    cj = 0;
+    if (++ckvh == Hkv) {
+      ckvh = 0;
+      do { cb++; } while (cb < B && prefix[cb + 1] == prefix[cb]);
+    }
+  }
+
+  if (timed_out) {
+    // Drain the loads this warp still has in flight (bounded) before exit.
+    for (int k = i + 1; k < min(nwork, i + STAGES); k++) {
+      const int slot = k % STAGES;
+      if (!mbar_wait(smem_u32(&wbars[slot]), (uint32_t)((k / STAGES) & 1), a.status)) break;
+    }
+  }
+}
+
+// ------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+constexpr int kWarps = 8;
+constexpr int kStages = 3;
+
+}  // namespace
+
+namespace zl {
+
+// 2-D bf16 tensor map over `rows` rows of `cols` elements (row pitch
+// `pitch_bytes`), box [box_rows][box_cols], 128-byte swizzle.
+zl_status make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows,
+                         uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(ZL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ZL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %llu x %llu", (int)r,
+                     (unsigned long long)rows, (unsigned long long)cols);
+  return ZL_OK;
+}
+
+zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool, const void* v_pool,
+                                  const int32_t* block_tables, const int32_t* seq_lens, void* out,
+                                  int B, int H, int Hkv, int d, int bs, int max_blocks,
+                                  int64_t num_blocks, float scale, zl_gqa_map map, int num_splits,
+                                  cudaStream_t st) {
+  (void)num_splits;
+  if (d != D || bs != BS || Hkv <= 0 || H % Hkv != 0 || H / Hkv > MAX_G || B > MAX_B ||
+      map != ZL_GQA_GROUPED && H != Hkv)
+    return ZL_ERR_UNSUPPORTED;
+  const uint64_t rows = (uint64_t)num_blocks * Hkv * BS;
+  if (rows == 0 || rows >= (1ull << 31)) return ZL_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return ZL_ERR_UNSUPPORTED;
+  if (B == 0) return ZL_OK;
+
+  CUtensorMap tk, tv;
+  zl_status s = make_tmap_bf16(&tk, k_pool, D, rows, D * 2, 64, BS);
+  if (s != ZL_OK) return s;
+  s = make_tmap_bf16(&tv, v_pool, D, rows, D * 2, 64, BS);
+  if (s != ZL_OK) return s;
+
+  const int grid = ctx->num_sms;
+  const int64_t W = (int64_t)grid * kWarps;
+  s = ensure_workspace(ctx, sizeof(Partial) * 2 * W);
+  if (s != ZL_OK) return s;
+  s = ensure_counters(ctx, sizeof(int) * (size_t)B * Hkv);
+  if (s != ZL_OK) return s;
+
+  DecodeArgs args;
+  args.q = (const __nv_bfloat16*)q;
+  args.block_tables = block_tables;
+  args.seq_lens = seq_lens;
+  args.out = (__nv_bfloat16*)out;
+  args.partials = (Partial*)ctx->workspace;
+  args.counters = (int*)ctx->counters;
+  args.status = ctx->d_status;
+  args.B = B; args.H = H; args.Hkv = Hkv; args.G = H / Hkv; args.max_blocks = max_blocks;
+  args.num_blocks = num_blocks;
+  args.scale_log2 = scale * LOG2E;
+
+  using SM = Smem<kWarps, kStages>;
+  auto kern = paged_decode_bf16_kernel<kWarps, kStages>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    ZL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal));
+    attr_set = true;
+  }
+  kern<<<grid, kWarps * 32, SM::kTotal, st>>>(args, tk, tv);
+  ZL_LAUNCH_CHECK(ctx);
+  return ZL_OK;
+}
+
+}  // namespace zl

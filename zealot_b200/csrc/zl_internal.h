@@ -1,0 +1,109 @@
+// zl_internal.h -- shared host-side state and helpers of libzealot_attn.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/zealot_attn.h"
+
+// Bits of the per-context device status word (kernels atomicOr them).
+enum : int {
+  ZL_DEV_OOB = 1,      // block id / slot outside the pool, or table overflow
+  ZL_DEV_TIMEOUT = 2,  // a bounded wait gave up
+};
+
+struct zl_ctx {
+  int device = 0;
+  int num_sms = 148;
+  int* d_status = nullptr;        // device status word
+  void* workspace = nullptr;      // split-KV partials + per-segment counters
+  size_t workspace_bytes = 0;
+  void* counters = nullptr;       // zeroed int32 counters, self-resetting
+  size_t counters_bytes = 0;
+  std::atomic<uint64_t> launches{0};
+  // NCCL (loaded at run time)
+  void* nccl_comm = nullptr;
+  int nranks = 1, rank = 0;
+  void* gather_buf = nullptr;
+  size_t gather_bytes = 0;
+};
+
+namespace zl {
+
+zl_status set_error(zl_status s, const char* fmt, ...);
+inline zl_status ok() { return ZL_OK; }
+
+// Makes the context's device current; returns ZL_ERR_CUDA on failure.
+zl_status bind_device(zl_ctx* ctx);
+
+// Grows the context workspace (stream-ordered free of the old one is not
+// needed: callers synchronise through the stream they pass).
+zl_status ensure_workspace(zl_ctx* ctx, size_t bytes);
+zl_status ensure_counters(zl_ctx* ctx, size_t bytes);
+
+inline cudaStream_t S(zl_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+
+#define ZL_CUDA_TRY(expr)                                                            \
+  do {                                                                               \
+    cudaError_t _e = (expr);                                                         \
+    if (_e != cudaSuccess)                                                           \
+      return ::zl::set_error(ZL_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,            \
+                             cudaGetErrorString(_e), __FILE__, __LINE__);            \
+  } while (0)
+
+#define ZL_LAUNCH_CHECK(ctx)                                                         \
+  do {                                                                               \
+    cudaError_t _e = cudaGetLastError();                                             \
+    if (_e != cudaSuccess)                                                           \
+      return ::zl::set_error(ZL_ERR_CUDA, "kernel launch failed: %s (%s:%d)",       \
+                             cudaGetErrorString(_e), __FILE__, __LINE__);            \
+    (ctx)->launches.fetch_add(1, std::memory_order_relaxed);                         \
+  } while (0)
+
+inline size_t dtype_size(zl_dtype t) { return t == ZL_F32 ? 4 : 2; }
+inline bool dtype_ok(zl_dtype t) { return t == ZL_F32 || t == ZL_BF16; }
+
+// Internal launchers shared between translation units.
+zl_status launch_decode_generic(zl_ctx* ctx, const void* q, const void* k_pool,
+                                const void* v_pool, const int32_t* block_tables,
+                                const int32_t* seq_lens, const int32_t* tok_begin,
+                                void* out, float* m_out, float* l_out, float* o_out,
+                                int B, int H, int Hkv, int d, int bs, int max_blocks,
+                                int64_t num_blocks, float scale, zl_gqa_map map,
+                                zl_dtype dtype, cudaStream_t st);
+zl_status launch_prefill_generic(zl_ctx* ctx, const void* q, const void* k, const void* v,
+                                 const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
+                                 void* out, int H, int Hkv, int d, float scale, int causal,
+                                 zl_gqa_map map, zl_dtype dtype, cudaStream_t st);
+// Fast bf16 decode (paged_decode_bf16.cu). Returns ZL_ERR_UNSUPPORTED when the
+// shape is outside its envelope so the caller can use the CUDA-core kernel.
+zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool,
+                                  const void* v_pool, const int32_t* block_tables,
+                                  const int32_t* seq_lens, void* out, int B, int H, int Hkv,
+                                  int d, int bs, int max_blocks, int64_t num_blocks, float scale,
+                                  zl_gqa_map map, int num_splits, cudaStream_t st);
+zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const void* v,
+                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len, void* out,
+                            int H, int Hkv, int d, float scale, int causal, zl_gqa_map map,
+                            cudaStream_t st);
+zl_status launch_merge(zl_ctx* ctx, const float* m, const float* l, const float* o, int P,
+                       int64_t rows, int d, void* out, zl_dtype dtype, cudaStream_t st);
+zl_status launch_embedding_gather(zl_ctx* ctx, const int64_t* ids, int64_t n, const float* table,
+                                  int64_t vocab, int hidden, float* out, cudaStream_t st);
+zl_status launch_matmul_f32(zl_ctx* ctx, const float* a, const float* b, float* c, int64_t m,
+                            int64_t k, int64_t n, cudaStream_t st);
+zl_status launch_gather_rows_f32(zl_ctx* ctx, const float* src, const int32_t* rows, int64_t n,
+                                 int64_t width, float* dst, cudaStream_t st);
+
+// Default softmax scale 1/sqrt(d) computed like src/attention/mod.rs:53.
+inline float resolve_scale(float scale, int d) {
+  return scale > 0.f ? scale : 1.0f / sqrtf((float)d);
+}
+
+}  // namespace zl
