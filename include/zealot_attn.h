@@ -141,11 +141,14 @@ zl_status zl_merge_partials(zl_ctx* ctx, const float* m, const float* l, const f
 /* Replaces CudaAttention::forward_gpu (src/attention/cuda.rs:56-110) and
  * tiled_attention_kernel (attention.cu:9-187). Packed varlen layout instead of
  * one [H][L][d] sequence: q/out [T][H][d], k/v [T][Hkv][d], cu_seqlens
- * [num_seqs+1] int32 (device), T = cu_seqlens[num_seqs]; max_seq_len bounds the
- * launch. causal != 0 masks keys after the query. bf16 with head_dim 128 runs
- * on the tcgen05/TMEM tensor-core kernel; other shapes on the CUDA-core kernel. */
+ * [num_seqs+1] int32 (device) with cu_seqlens[num_seqs] == total_tokens == T
+ * (the row count of the buffers, which bounds every tile load); max_seq_len
+ * bounds the launch. causal != 0 masks keys after the query. bf16 with
+ * head_dim 128 and an even GQA group runs on the tcgen05/TMEM tensor-core
+ * kernel; other shapes on the CUDA-core kernel. */
 zl_status zl_prefill_varlen(zl_ctx* ctx, const void* q, const void* k, const void* v,
-                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len, void* out,
+                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
+                            int64_t total_tokens, void* out,
                             int num_heads, int num_kv_heads, int head_dim, float scale, int causal,
                             zl_gqa_map gqa_map, zl_dtype dtype, zl_stream stream);
 

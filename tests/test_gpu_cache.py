@@ -14,7 +14,7 @@ def test_reshape_and_cache_bit_exact(ctx, oracle, dtype, Hkv, d, bs):
     import torch
     import zealot_b200 as zb
     rng = np.random.default_rng(Hkv * 100 + d)
-    nb, T = 64, 300
+    nb, T = 128, 300
     k = rng.standard_normal((T, Hkv, d)).astype(np.float32)
     v = rng.standard_normal((T, Hkv, d)).astype(np.float32)
     slots = rng.permutation(nb * bs)[:T].astype(np.int64)

@@ -64,8 +64,8 @@ SIGNATURES = {
     "zl_merge_partials": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int,
                                   c_void_p, c_int, c_void_p]),
     "zl_prefill_varlen": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
-                                  c_void_p, c_int, c_int, c_int, c_float, c_int, c_int, c_int,
-                                  c_void_p]),
+                                  c_int64, c_void_p, c_int, c_int, c_int, c_float, c_int, c_int,
+                                  c_int, c_void_p]),
     "zl_nccl_get_unique_id": (c_int, [c_void_p]),
     "zl_nccl_init": (c_int, [c_void_p, c_void_p, c_int, c_int]),
     "zl_nccl_merge": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,

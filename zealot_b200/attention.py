@@ -97,7 +97,10 @@ class CudaAttention:
         for t in (q, k, v, cu_seqlens, o):
             _need(t.is_contiguous() and t.is_cuda, "tensors must be contiguous CUDA tensors")
         n = cu_seqlens.numel() - 1
+        T = q.shape[0]
+        _need(q.numel() == T * num_heads * head_dim and k.numel() == T * num_kv_heads * head_dim
+              and v.numel() == k.numel() and o.numel() == q.numel(), "q/k/v/o shapes")
         check(self.lib.zl_prefill_varlen(self.ctx.handle, ptr(q), ptr(k), ptr(v), ptr(cu_seqlens), n,
-                                         max_seq_len, ptr(o), num_heads, num_kv_heads, head_dim, scale,
+                                         max_seq_len, T, ptr(o), num_heads, num_kv_heads, head_dim, scale,
                                          int(causal), gqa_map, dtype_code(q.dtype),
                                          self.ctx.stream(stream)))

@@ -147,6 +147,10 @@ zl_status zl_check_status(zl_ctx* ctx, zl_stream stream) {
   int h = 0;
   ZL_CUDA_TRY(cudaMemcpy(&h, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
   ZL_CUDA_TRY(cudaMemset(ctx->d_status, 0, sizeof(int)));
+  if (h && ctx->counters) {
+    // A kernel that gave up may have left split-KV counters mid-count.
+    ZL_CUDA_TRY(cudaMemset(ctx->counters, 0, ctx->counters_bytes));
+  }
   if (h & ZL_DEV_TIMEOUT) return set_error(ZL_ERR_TIMEOUT, "a bounded device wait ran out (status 0x%x)", h);
   if (h & ZL_DEV_OOB)
     return set_error(ZL_ERR_OOB_BLOCK, "a block id or slot was outside the pool (status 0x%x)", h);

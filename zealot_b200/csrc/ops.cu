@@ -82,22 +82,23 @@ zl_status zl_merge_partials(zl_ctx* ctx, const float* m, const float* l, const f
 }
 
 zl_status zl_prefill_varlen(zl_ctx* ctx, const void* q, const void* k, const void* v,
-                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len, void* out,
+                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
+                            int64_t total_tokens, void* out,
                             int num_heads, int num_kv_heads, int head_dim, float scale, int causal,
                             zl_gqa_map gqa_map, zl_dtype dtype, zl_stream stream) {
   zl_status s = bind_device(ctx);
   if (s != ZL_OK) return s;
   if (!dtype_ok(dtype)) return set_error(ZL_ERR_INVALID_ARG, "prefill_varlen: bad dtype");
   if ((s = check_heads(num_heads, num_kv_heads, head_dim, "prefill_varlen")) != ZL_OK) return s;
-  if (num_seqs < 0 || max_seq_len < 0)
+  if (num_seqs < 0 || max_seq_len < 0 || total_tokens < 0)
     return set_error(ZL_ERR_INVALID_ARG, "prefill_varlen: bad sizes");
-  if (num_seqs == 0 || max_seq_len == 0) return ZL_OK;
+  if (num_seqs == 0 || max_seq_len == 0 || total_tokens == 0) return ZL_OK;
   if (!q || !k || !v || !cu_seqlens || !out)
     return set_error(ZL_ERR_INVALID_ARG, "prefill_varlen: null pointer");
   const float sc = resolve_scale(scale, head_dim);
   cudaStream_t st = S(stream);
   if (dtype == ZL_BF16) {
-    s = launch_prefill_tc(ctx, q, k, v, cu_seqlens, num_seqs, max_seq_len, out, num_heads,
+    s = launch_prefill_tc(ctx, q, k, v, cu_seqlens, num_seqs, max_seq_len, total_tokens, out, num_heads,
                           num_kv_heads, head_dim, sc, causal, gqa_map, st);
     if (s != ZL_ERR_UNSUPPORTED) return s;
   }

@@ -100,6 +100,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   const int lane = tid & 31;
   const int B = a.B, Hkv = a.Hkv;
 
+  if (aborted(a.status)) return;  // an earlier launch timed out and was not cleared
   if (tid == 0) {
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
@@ -150,8 +151,12 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
 
   const int64_t NB = prefix[B];         // sum of blocks over sequences
   const int64_t TB = NB * Hkv;          // flat work items
-  const int64_t W = (int64_t)gridDim.x * WARPS;
+  // Active warps: never more than work items, so every warp in [0, W) owns at
+  // least one block and the contributors of a split (sequence, kv head) are
+  // exactly the consecutive warps owner_warp(first block) .. owner_warp(last).
+  const int64_t W = min((int64_t)gridDim.x * WARPS, TB);
   const int gw = blockIdx.x * WARPS + warp;
+  if (gw >= W) return;
 
   // Sequences with no context produce zeros (CTA 0 writes them).
   if (blockIdx.x == 0) {
@@ -292,7 +297,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     for (int j = seg_j0; j < seg_jend; j++, i++) {
       const int slot = i % STAGES;
       const uint32_t bar = smem_u32(&wbars[slot]);
-      if (!mbar_wait(bar, (uint32_t)((i / STAGES) & 1), a.status)) {
+      if (!mbar_wait_warp(bar, (uint32_t)((i / STAGES) & 1), a.status)) {
         timed_out = true;
         break;
       }
@@ -455,7 +460,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     // Drain the loads this warp still has in flight (bounded) before exit.
     for (int k = i + 1; k < min(nwork, i + STAGES); k++) {
       const int slot = k % STAGES;
-      if (!mbar_wait(smem_u32(&wbars[slot]), (uint32_t)((k / STAGES) & 1), a.status)) break;
+      if (!mbar_wait_warp(smem_u32(&wbars[slot]), (uint32_t)((k / STAGES) & 1), a.status)) break;
     }
   }
 }

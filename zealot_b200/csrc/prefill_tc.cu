@@ -1,17 +1,329 @@
-// prefill_tc.cu -- varlen causal prefill on tcgen05 tensor cores (placeholder
-// until the kernel lands: reports the shape as unsupported so the CUDA-core
-// kernel runs).
+// prefill_tc.cu -- variable-length causal prefill attention on the sm_100a
+// tensor cores (tcgen05 + TMEM, fed by TMA), bf16 in, fp32 accumulate.
+//
+// Replaces tiled_attention_kernel (src/attention/kernels/attention.cu:9-187
+// of the reference: scalar fp32 FMAs over shared memory, one sequence in
+// [H][L][d]) for packed varlen input q [T][H][128], k/v [T][Hkv][128].
+//
+// One CTA owns a 128-row query tile of one sequence for TWO query heads of the
+// same kv group, so every K/V tile it loads feeds two score tiles:
+//   warp 0      TMA producer: Q tiles once, K/V tiles through a 2-stage ring
+//   warp 1      MMA issuer (one thread) + TMEM owner (alloc/dealloc 512 cols)
+//   warps 4-7   softmax warpgroup for head 0, one thread per query row
+//   warps 8-11  softmax warpgroup for head 1
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); the bf16
+// probabilities P overwrite the first 64 columns of their S tile and feed
+// O += P V straight from TMEM. The MMA warp interleaves the two heads
+// (PV0(j), S0(j+1), PV1(j), S1(j+1)) so one warpgroup's softmax overlaps the
+// other's matrix products. Causal tiles past the diagonal are never loaded.
+// Every mbarrier wait is bounded (status word + unwind instead of a hang).
 #include "zl_internal.h"
+#include "zl_ptx.cuh"
+
+namespace zl {
+zl_status make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t cols, uint64_t rows,
+                         uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows);
+}
+
+namespace {
+
+using namespace zl::ptx;
+
+constexpr int D = 128;
+constexpr int BM = 128;                 // query rows per tile
+constexpr int BN = 128;                 // keys per tile
+constexpr int NQ = 2;                   // query heads per CTA
+constexpr int TILE = BM * D * 2;        // 32 KB (two 16 KB swizzled boxes)
+constexpr int HALF = TILE / 2;
+constexpr int THREADS = 384;
+constexpr float LOG2E = 1.4426950408889634f;
+
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_READY = 11,
+           O_FINAL = 13, NUM_BARS = 15 };
+
+struct Smem {
+  static constexpr int kQ = 0;                      // NQ tiles
+  static constexpr int kK = kQ + NQ * TILE;         // 2 stages
+  static constexpr int kV = kK + 2 * TILE;          // 2 stages
+  static constexpr int kBars = kV + 2 * TILE;
+  static constexpr int kTmem = kBars + NUM_BARS * 8;
+  static constexpr int kTotal = 1024 + kTmem + 16;
+};
+
+struct PrefillArgs {
+  const int32_t* cu_seqlens;
+  __nv_bfloat16* out;  // [T][H][D]
+  int* status;
+  int H, Hkv, G, num_seqs;
+  float scale_log2;
+  int causal;
+};
+
+constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
+constexpr uint32_t IDESC_PV = idesc_bf16(BM, D, false, true);
+
+// K-major, 128-byte swizzle operand (Q or K tile): k-step kk covers 16 of the
+// 128 head dims; dims 0-63 live in the first 16 KB box, 64-127 in the second.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
+  return sdesc(tile + (kk >> 2) * HALF + (kk & 3) * 32, 16, 1024, 2);
+}
+// MN-major, 128-byte swizzle B operand (V tile as [keys][dims]): k-step kk
+// covers keys 16kk..16kk+15; the two 64-dim boxes are LBO = 16 KB apart.
+__device__ __forceinline__ uint64_t desc_v(uint32_t tile, int kk) {
+  return sdesc(tile + kk * 2048, HALF, 1024, 2);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
+                  const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV) {
+  const int hp_count = a.H / NQ;
+  const int s = blockIdx.x / hp_count;
+  const int hp = blockIdx.x - s * hp_count;
+  const int t = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles launch first
+  const int start = a.cu_seqlens[s];
+  const int L = a.cu_seqlens[s + 1] - start;
+  if (BM * t >= L) return;  // uniform: this tile is past the sequence
+  if (aborted(a.status)) return;  // an earlier CTA timed out: do not queue behind it
+  const int h0 = hp * NQ;
+  const int kvh = h0 / a.G;
+  const int nkv = a.causal ? t + 1 : (L + BN - 1) / BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sbase = smem_raw + (base - raw);
+  auto bar = [&](int i) { return base + Smem::kBars + 8 * i; };
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sbase + Smem::kTmem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NUM_BARS; i++) {
+      const int count = (i == P_READY || i == P_READY + 1) ? 128 : 1;
+      mbar_init(bar(i), count);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    __syncwarp();  // tcgen05.alloc/dealloc are warp-collective (.sync.aligned)
+    tmem_alloc(base + Smem::kTmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO[2] = {tmem + 256, tmem + 384};
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------- producer
+    const int y0 = start + BM * t;
+    mbar_arrive_expect_tx(bar(Q_FULL), NQ * TILE);
+    for (int w = 0; w < NQ; w++) {
+      const uint32_t dst = base + Smem::kQ + w * TILE;
+      tma_load_2d(dst, &tmQ, (h0 + w) * D, y0, bar(Q_FULL));
+      tma_load_2d(dst + HALF, &tmQ, (h0 + w) * D + 64, y0, bar(Q_FULL));
+    }
+    for (int j = 0; j < nkv; j++) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      const int y = start + BN * j;
+      if (!mbar_wait(bar(K_EMPTY + st), ph ^ 1, a.status)) break;
+      mbar_arrive_expect_tx(bar(K_FULL + st), TILE);
+      tma_load_2d(base + Smem::kK + st * TILE, &tmK, kvh * D, y, bar(K_FULL + st));
+      tma_load_2d(base + Smem::kK + st * TILE + HALF, &tmK, kvh * D + 64, y, bar(K_FULL + st));
+      if (!mbar_wait(bar(V_EMPTY + st), ph ^ 1, a.status)) break;
+      mbar_arrive_expect_tx(bar(V_FULL + st), TILE);
+      tma_load_2d(base + Smem::kV + st * TILE, &tmV, kvh * D, y, bar(V_FULL + st));
+      tma_load_2d(base + Smem::kV + st * TILE + HALF, &tmV, kvh * D + 64, y, bar(V_FULL + st));
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ----------------------------------------------------------- MMA issuer
+    auto issue_s = [&](int w, int st) {
+      const uint32_t q = base + Smem::kQ + w * TILE;
+      const uint32_t k = base + Smem::kK + st * TILE;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk++)
+        tc_mma_ss(tS[w], desc_kmajor(q, kk), desc_kmajor(k, kk), IDESC_S, kk > 0);
+    };
+    auto issue_pv = [&](int w, int st, bool acc) {
+      const uint32_t v = base + Smem::kV + st * TILE;
+#pragma unroll
+      for (int kk = 0; kk < BN / 16; kk++)
+        tc_mma_ts(tO[w], tS[w] + kk * 8, desc_v(v, kk), IDESC_PV, (acc || kk > 0) ? 1u : 0u);
+    };
+    bool ok = mbar_wait(bar(Q_FULL), 0, a.status) && mbar_wait(bar(K_FULL), 0, a.status);
+    if (ok) {
+      tc_fence_after();
+      for (int w = 0; w < NQ; w++) {
+        issue_s(w, 0);
+        tc_commit(bar(S_FULL + w));
+      }
+      tc_commit(bar(K_EMPTY));
+    }
+    for (int j = 0; ok && j < nkv; j++) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      const int st1 = (j + 1) & 1;
+      const uint32_t ph1 = ((j + 1) >> 1) & 1;
+      if (!(ok = mbar_wait(bar(V_FULL + st), ph, a.status))) break;
+      for (int w = 0; w < NQ && ok; w++) {
+        if (!(ok = mbar_wait(bar(P_READY + w), j & 1, a.status))) break;
+        tc_fence_after();
+        issue_pv(w, st, j > 0);
+        if (w == NQ - 1) tc_commit(bar(V_EMPTY + st));
+        if (j + 1 < nkv) {
+          if (w == 0 && !(ok = mbar_wait(bar(K_FULL + st1), ph1, a.status))) break;
+          tc_fence_after();
+          issue_s(w, st1);
+          tc_commit(bar(S_FULL + w));
+          if (w == NQ - 1) tc_commit(bar(K_EMPTY + st1));
+        } else {
+          tc_commit(bar(O_FINAL + w));
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------ softmax + epilogue
+    const int w = (warp - 4) >> 2;             // which query head of the pair
+    const int r = 32 * (warp & 3) + lane;      // query row in the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+    const uint32_t tSr = tS[w] + lane_off, tOr = tO[w] + lane_off;
+    const int q_row = BM * t + r;              // row index within the sequence
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; j++) {
+      if (!(ok = mbar_wait_warp(bar(S_FULL + w), j & 1, a.status))) break;
+      tc_fence_after();
+      const int key0 = BN * j;
+      const bool edge = (j == nkv - 1);
+      // keys valid for this row: < key_lim
+      const int key_lim = edge ? (a.causal ? min(q_row + 1, L) : L) - key0 : BN;
+      uint32_t v[32];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        tmem_ld32(tSr + 32 * c, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const float x = __uint_as_float(v[i]);
+          mx = (32 * c + i < key_lim) ? fmaxf(mx, x) : mx;
+        }
+      }
+      const float m_new = fmaxf(m, mx * a.scale_log2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_use);
+      float lsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        tmem_ld32(tSr + 32 * c, v);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int k0 = 32 * c + 2 * i;
+          const float p0 = (k0 < key_lim) ? ex2(__uint_as_float(v[2 * i]) * a.scale_log2 - m_use) : 0.f;
+          const float p1 = (k0 + 1 < key_lim) ? ex2(__uint_as_float(v[2 * i + 1]) * a.scale_log2 - m_use) : 0.f;
+          lsum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tSr + 16 * c, pk);
+      }
+      l = l * alpha + lsum;
+      // tcgen05.ld/st are warp-collective: the rescale branch must be taken by
+      // the whole warp (rows whose max did not move multiply by alpha == 1).
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          tmem_ld32(tOr + 32 * c, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st32(tOr + 32 * c, v);
+        }
+      }
+      m = m_new;
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(P_READY + w));
+    }
+    if (ok && mbar_wait_warp(bar(O_FINAL + w), 0, a.status)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool row_ok = q_row < L;
+      uint4* dst = reinterpret_cast<uint4*>(a.out + ((int64_t)(start + q_row) * a.H + h0 + w) * D);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        uint32_t v[32];
+        tmem_ld32(tOr + 32 * c, v);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+          pk[i] = pack_bf16x2(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv);
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            dst[4 * c + i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+    }
+  }
+  __syncwarp();  // lanes of warps 0 and 1 arrive from different roles
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // lane 0 arrives here from the MMA role, lanes 1-31 from the barrier:
+    // reconverge the warp before the warp-collective dealloc.
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
 
 namespace zl {
 
 zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const void* v,
-                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len, void* out,
-                            int H, int Hkv, int d, float scale, int causal, zl_gqa_map map,
-                            cudaStream_t st) {
-  (void)ctx; (void)q; (void)k; (void)v; (void)cu_seqlens; (void)num_seqs; (void)max_seq_len;
-  (void)out; (void)H; (void)Hkv; (void)d; (void)scale; (void)causal; (void)map; (void)st;
-  return ZL_ERR_UNSUPPORTED;
+                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
+                            int64_t total_tokens, void* out, int H, int Hkv, int d, float scale,
+                            int causal, zl_gqa_map map, cudaStream_t st) {
+  if (d != D || Hkv <= 0 || H % Hkv != 0 || (H / Hkv) % NQ != 0 || total_tokens <= 0 ||
+      (map != ZL_GQA_GROUPED && H != Hkv) || (H / Hkv) < NQ)
+    return ZL_ERR_UNSUPPORTED;
+  if (total_tokens >= (1ll << 31) || num_seqs > 0x7fffffff / (H / NQ)) return ZL_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return ZL_ERR_UNSUPPORTED;
+  const int max_tiles = (max_seq_len + BM - 1) / BM;
+  if (max_tiles > 65535) return ZL_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk, tv;
+  zl_status s = make_tmap_bf16(&tq, q, (uint64_t)H * D, total_tokens, (uint64_t)H * D * 2, 64, BM);
+  if (s != ZL_OK) return s;
+  if ((s = make_tmap_bf16(&tk, k, (uint64_t)Hkv * D, total_tokens, (uint64_t)Hkv * D * 2, 64, BN)) != ZL_OK) return s;
+  if ((s = make_tmap_bf16(&tv, v, (uint64_t)Hkv * D, total_tokens, (uint64_t)Hkv * D * 2, 64, BN)) != ZL_OK) return s;
+  PrefillArgs args;
+  args.cu_seqlens = cu_seqlens;
+  args.out = (__nv_bfloat16*)out;
+  args.status = ctx->d_status;
+  args.H = H; args.Hkv = Hkv; args.G = H / Hkv; args.num_seqs = num_seqs;
+  args.scale_log2 = scale * LOG2E;
+  args.causal = causal ? 1 : 0;
+  static bool attr = false;
+  if (!attr) {
+    ZL_CUDA_TRY(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Smem::kTotal));
+    attr = true;
+  }
+  dim3 grid((unsigned)(num_seqs * (H / NQ)), (unsigned)max_tiles);
+  prefill_tc_kernel<<<grid, THREADS, Smem::kTotal, st>>>(args, tq, tk, tv);
+  ZL_LAUNCH_CHECK(ctx);
+  return ZL_OK;
 }
 
 }  // namespace zl

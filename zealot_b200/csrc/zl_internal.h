@@ -89,7 +89,8 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
                                   int d, int bs, int max_blocks, int64_t num_blocks, float scale,
                                   zl_gqa_map map, int num_splits, cudaStream_t st);
 zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const void* v,
-                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len, void* out,
+                            const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
+                            int64_t total_tokens, void* out,
                             int H, int Hkv, int d, float scale, int causal, zl_gqa_map map,
                             cudaStream_t st);
 zl_status launch_merge(zl_ctx* ctx, const float* m, const float* l, const float* o, int P,

@@ -28,26 +28,52 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// Non-blocking probe of a phase (mbarrier.test_wait never suspends the
+// thread, so the polling loop below always regains control).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
-// ~1 s at B200 clocks before giving up.
+// ~1 s at B200 clocks before giving up. While waiting, the status word is
+// polled: once any thread of any CTA has timed out, every other wait gives up
+// at once, so a systematic failure costs about one second, not one per wait.
 constexpr long long kWaitCycles = 2000000000LL;
+__device__ __forceinline__ bool aborted(const int* status) {
+  return (*reinterpret_cast<const volatile int*>(status) & 2 /* ZL_DEV_TIMEOUT */) != 0;
+}
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t it = 1;; it++) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (it > 64) __nanosleep(32);
+    if ((it & 255) == 0 && aborted(status)) return false;
     if (clock64() - t0 > kWaitCycles) {
       atomicOr(status, 2 /* ZL_DEV_TIMEOUT */);
+      return false;
+    }
+  }
+}
+
+// Whole-warp form: all 32 lanes poll together and leave the loop in the same
+// iteration, so the warp is converged for the .sync.aligned instructions that
+// follow (ldmatrix, mma.sync, tcgen05.ld/st). Returns a warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* status) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0;; it++) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if (it > 64) __nanosleep(32);
+    const bool ab = (it & 255) == 255 && aborted(status);
+    const bool to = clock64() - t0 > kWaitCycles;
+    if (__any_sync(0xffffffffu, ab || to)) {
+      if (to && (threadIdx.x & 31) == 0) atomicOr(status, 2 /* ZL_DEV_TIMEOUT */);
       return false;
     }
   }
