@@ -116,6 +116,31 @@ zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const 
                           int block_size, int max_blocks_per_seq, int64_t num_blocks, float scale,
                           zl_gqa_map gqa_map, int num_splits, zl_dtype dtype, zl_stream stream);
 
+/* Allocation-free paged decode. No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory while they serve -- an
+ * engine that hands (nearly) all HBM to its KV-cache pool at start-up has
+ * nothing left for the on-demand workspace zl_paged_decode grows with
+ * cudaMalloc, and a step loop that must not stall cannot take the
+ * device-wide synchronisation cudaMalloc/cudaFree imply. Same kernel and
+ * results as zl_paged_decode for bf16, head_dim 128, block_size 16, grouped
+ * GQA with <= 8 query heads per kv head; no zl_ctx, the current device is
+ * used. Its split-KV scratch is a static device array of about 10.7 MB that
+ * every GPU which loads the library holds until the process exits. Limits:
+ * num_seqs <= 4096 and num_seqs * num_kv_heads <= 16384, else
+ * ZL_ERR_INVALID_ARG; other shapes return ZL_ERR_UNSUPPORTED. The first call
+ * on a device resolves the array's device address and sets the kernel's
+ * shared-memory limit, so make that first call before any stream capture.
+ * All calls share the array: calls whose kernels overlap on the GPU race and
+ * give wrong results; calls ordered on one stream are safe. status (device,
+ * optional, caller-cleared): the kernel ORs 1 (block id outside the pool)
+ * and 2 (a bounded wait ran out) into it; while bit 2 is set the kernel
+ * returns without work. */
+zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                  const int32_t* block_tables, const int32_t* seq_lens, void* out,
+                                  int* status, int num_seqs, int num_heads, int num_kv_heads,
+                                  int head_dim, int block_size, int max_blocks_per_seq,
+                                  int64_t num_blocks, float scale, zl_stream stream);
+
 /* Sequence-split form (one sequence's KV spread over GPUs): attends only to
  * tokens [tok_begin[b], tok_end[b]) of each sequence (tok_begin may be NULL =
  * 0) and writes the unnormalised partial triple per (b, h):

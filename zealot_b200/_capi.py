@@ -57,6 +57,9 @@ SIGNATURES = {
     "zl_paged_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int64,
                                 c_float, c_int, c_int, c_int, c_void_p]),
+    "zl_paged_decode_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                        c_int, c_int64, c_float, c_void_p]),
     "zl_paged_decode_partial": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                         c_int, c_int, c_int, c_int, c_int, c_int64, c_float, c_int,

@@ -560,3 +560,144 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
 }
 
 }  // namespace zl
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// zl_paged_decode keeps its split-KV partials and merge counters in a context
+// workspace that it grows with cudaMalloc on first use and whenever a batch
+// needs more. Some callers cannot allow that: a serving engine that hands
+// (nearly) all HBM to its KV-cache pool at start-up has nothing left for an
+// on-demand allocation, and a step loop that must not stall cannot accept
+// the device-wide synchronisation cudaMalloc/cudaFree imply. For them,
+// zl_paged_decode_noalloc runs the same kernel with its scratch in the
+// file-scope array below, which is part of the loaded module: every GPU that
+// loads this library holds it (about 10.7 MB) until the process exits.
+//
+// Limits: bf16, head_dim 128, block_size 16, grouped GQA with at most 8
+// query heads per kv head, num_seqs <= 4096, num_seqs * num_kv_heads <=
+// kNoAllocMaxSegments. Larger requests are rejected with an error.
+// All calls share the array: two calls whose kernels overlap on the GPU (on
+// different streams, or from different host threads without ordering) race
+// on it and give wrong results. Calls ordered on one stream are safe; each
+// call clears the merge counters it uses before its kernel runs.
+namespace {
+
+constexpr int kNoAllocMaxCtas = 160;            // >= 148 SMs of a B200
+constexpr int kNoAllocMaxSegments = 16384;      // (sequence, kv head) pairs per call
+struct NoAllocScratch {
+  Partial partials[2 * kNoAllocMaxCtas * kWarps];
+  int status;                          // device flags when the caller passes no status word
+  int counters[kNoAllocMaxSegments];   // must directly follow `status` (cleared together)
+};
+static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
+
+constexpr int kMaxDevices = 64;
+struct NoAllocDevice {
+  NoAllocScratch* scratch = nullptr;  // device address of g_noalloc_scratch
+  int num_sms = 0;
+};
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: resolve the array's device
+// address (the host-side symbol is only a stand-in and must never be handed
+// to a kernel) and raise the kernel's dynamic shared-memory limit.
+zl_status noalloc_setup(int dev, NoAllocDevice** out) {
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  NoAllocDevice& nd = g_noalloc_dev[dev];
+  if (!nd.scratch) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                           cudaGetErrorString(e));
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess)
+      return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: SM count: %s", cudaGetErrorString(e));
+    using SM = Smem<kWarps, kStages>;
+    e = cudaFuncSetAttribute(paged_decode_bf16_kernel<kWarps, kStages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal);
+    if (e != cudaSuccess)
+      return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: shared-memory limit: %s",
+                           cudaGetErrorString(e));
+    nd.num_sms = sms;
+    nd.scratch = reinterpret_cast<NoAllocScratch*>(p);
+  }
+  *out = &nd;
+  return ZL_OK;
+}
+
+}  // namespace
+
+extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                             const int32_t* block_tables, const int32_t* seq_lens,
+                                             void* out, int* status, int num_seqs, int num_heads,
+                                             int num_kv_heads, int head_dim, int block_size,
+                                             int max_blocks_per_seq, int64_t num_blocks,
+                                             float scale, zl_stream stream) {
+  using namespace zl;
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_blocks_per_seq < 0 || num_blocks < 0)
+    return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: bad sizes");
+  if (head_dim != D || block_size != BS || num_heads % num_kv_heads != 0 ||
+      num_heads / num_kv_heads > MAX_G)
+    return set_error(ZL_ERR_UNSUPPORTED,
+                     "paged_decode_noalloc: needs head_dim 128, block_size 16 and at most %d query "
+                     "heads per kv head (got d=%d bs=%d H=%d Hkv=%d)",
+                     MAX_G, head_dim, block_size, num_heads, num_kv_heads);
+  if (num_seqs > MAX_B || (int64_t)num_seqs * num_kv_heads > kNoAllocMaxSegments)
+    return set_error(ZL_ERR_INVALID_ARG,
+                     "paged_decode_noalloc: %d sequences x %d kv heads exceed the static scratch "
+                     "(at most %d sequences and %d sequence-kv-head pairs)",
+                     num_seqs, num_kv_heads, MAX_B, kNoAllocMaxSegments);
+  const uint64_t rows = (uint64_t)num_blocks * num_kv_heads * BS;
+  if (rows >= (1ull << 31))
+    return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: pool of %lld blocks is too large",
+                     (long long)num_blocks);
+  if (num_seqs == 0) return ZL_OK;
+  if (!q || !k_pool || !v_pool || !block_tables || !seq_lens || !out || rows == 0)
+    return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: null pointer or empty pool");
+  if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: pools and out must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(ZL_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  NoAllocDevice* nd = nullptr;
+  zl_status s = noalloc_setup(dev, &nd);
+  if (s != ZL_OK) return s;
+
+  CUtensorMap tk, tv;
+  if ((s = make_tmap_bf16(&tk, k_pool, D, rows, D * 2, 64, BS)) != ZL_OK) return s;
+  if ((s = make_tmap_bf16(&tv, v_pool, D, rows, D * 2, 64, BS)) != ZL_OK) return s;
+
+  cudaStream_t st = S(stream);
+  NoAllocScratch* scr = nd->scratch;
+  // The merge counters (and the fallback status word in front of them) must
+  // start at zero; clearing them per call also recovers from a call whose
+  // kernel gave up part-way.
+  e = cudaMemsetAsync(&scr->status, 0, sizeof(int) * (1 + (size_t)num_seqs * num_kv_heads), st);
+  if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: counter clear: %s", cudaGetErrorString(e));
+
+  DecodeArgs args;
+  args.q = (const __nv_bfloat16*)q;
+  args.block_tables = block_tables;
+  args.seq_lens = seq_lens;
+  args.out = (__nv_bfloat16*)out;
+  args.partials = scr->partials;
+  args.counters = scr->counters;
+  // Without a caller status word, device-side flags land in the scratch one.
+  args.status = status ? status : &scr->status;
+  args.B = num_seqs; args.H = num_heads; args.Hkv = num_kv_heads; args.G = num_heads / num_kv_heads;
+  args.max_blocks = max_blocks_per_seq;
+  args.num_blocks = num_blocks;
+  args.scale_log2 = resolve_scale(scale, D) * LOG2E;
+  const int grid = nd->num_sms < kNoAllocMaxCtas ? nd->num_sms : kNoAllocMaxCtas;
+  using SM = Smem<kWarps, kStages>;
+  paged_decode_bf16_kernel<kWarps, kStages><<<grid, kWarps * 32, SM::kTotal, st>>>(args, tk, tv);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: launch: %s", cudaGetErrorString(e));
+  return ZL_OK;
+}
