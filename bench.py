@@ -46,14 +46,14 @@ def log(*a):
 
 # ------------------------------------------------------------------ workload
 
-def make_lens_tables(world: int):
+def make_lens_tables(world: int, pool_blocks: int = NUM_BLOCKS):
     """Context lengths and block tables of the global batch (identical on every rank)."""
     rng = np.random.default_rng(SEED)
     B = B_PER_GPU * world
     lens = rng.integers(CTX_LO, CTX_HI + 1, size=B).astype(np.int32)
     nblk = (lens + BS - 1) // BS
-    # per rank the pool holds 65536 blocks of its own kv heads; the tables index it
-    pool_blocks = max(NUM_BLOCKS, int(nblk.sum()))
+    # per rank the pool holds its own kv heads' blocks; the tables index it
+    pool_blocks = max(pool_blocks, int(nblk.sum()))
     perm = rng.permutation(pool_blocks).astype(np.int32)
     tables = np.full((B, MAX_BLOCKS), -1, np.int32)
     off = 0
@@ -139,7 +139,7 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", dev))
 
-    lens, tables, pool_blocks = make_lens_tables(world)
+    lens, tables, pool_blocks = make_lens_tables(world, args.pool_blocks)
     B = len(lens)
     hkv_l, h_l = HKV // world, H // world  # this rank's kv-head group
     assert HKV % world == 0, "kv heads must divide over the GPUs"
@@ -183,7 +183,7 @@ def run_ours(args, rank, world, local_rank):
     # ~1 s of back-to-back steps so the sampler sees the GPU under this load; the
     # timed K steps follow immediately, inside the same sampling window.
     t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < 1.0:
+    while not args.lite and time.perf_counter() - t_soak < 1.0:
         for _ in range(20):
             step()
         stream.synchronize()
@@ -214,6 +214,8 @@ def run_ours(args, rank, world, local_rank):
     d2h = nbytes(hout)
 
     def e2e_step():
+        if args.lite:
+            return
         dq.copy_(hq, non_blocking=True)
         dtab.copy_(htab, non_blocking=True)
         dlen.copy_(hlen, non_blocking=True)
@@ -241,7 +243,7 @@ def run_ours(args, rank, world, local_rank):
     peaks = load_peaks()
     alg = algorithmic_bytes(lens, hkv_l, h_l)
     achieved = alg / (dev_ms / args.steps * 1e-3) / 1e9
-    traffic = load_traffic("decode_c2")
+    traffic = load_traffic("decode_c2_paged_decode_bf16")
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
             "algorithmic_bytes": alg, "peak_source": peaks["source"]}
@@ -285,6 +287,8 @@ def run_ours(args, rank, world, local_rank):
             "roofline": roof,
             "clocks": clk,
         }
+        if args.lite:
+            line["e2e"] = None
         line.update(side)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_single(lens, tables)
@@ -294,7 +298,7 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def side_measurements(ctx, attn, stream, peaks, args):
+def side_measurements(ctx, attn, stream, peaks, args, only=None):
     """C3 prefill TFLOPS and reshape_and_cache GB/s (1 GPU, same run)."""
     import torch
     res = {}
@@ -315,27 +319,35 @@ def side_measurements(ctx, attn, stream, peaks, args):
     def pre():
         attn.forward_gpu(q, k, v, tcu, o, H, HKV, D, int(lens.max()), causal=True, stream=sh)
 
-    n = 5
-    for _ in range(3):
+    n = getattr(args, "side_steps", 5)
+    for _ in range(args.warmup if only else 3):
+        if only == "cache":
+            break
         pre()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(n):
-        pre()
-    e1.record(stream)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / n
+    if only == "cache":
+        ms = float("nan")
+    else:
+        e0.record(stream)
+        for _ in range(n):
+            pre()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / n
     tf = flops / (ms * 1e-3) / 1e12
     res["prefill"] = {"workload": "C3 varlen causal prefill: 16 seqs, L U[256,8192], 32/8 heads, d 128, bf16",
                       "ms": round(ms, 4), "tflops": round(tf, 2), "peak_tflops": peaks["bf16_tflops"],
                       "frac": round(tf / peaks["bf16_tflops"], 4), "flop": flops}
+    if only == "prefill":
+        ctx.check_status(sh)
+        return res
     # reshape_and_cache of the same tokens into a pool via a random slot mapping
     nb = (T + BS - 1) // BS + 64
     with torch.cuda.stream(stream):
         pk = torch.empty((nb, HKV, BS, D), dtype=torch.bfloat16, device="cuda")
         pv = torch.empty_like(pk)
         slots = torch.from_numpy(rng.permutation(nb * BS)[:T].astype(np.int64)).cuda()
-    for _ in range(3):
+    for _ in range(args.warmup if only else 3):
         attn.reshape_and_cache(k, v, pk, pv, slots, HKV, D, BS, nb, stream=sh)
     e0.record(stream)
     for _ in range(n):
@@ -351,6 +363,27 @@ def side_measurements(ctx, attn, stream, peaks, args):
     return res
 
 
+def run_side_only(args):
+    """--workload prefill|cache: one side kernel on its C3 workload, own JSON line."""
+    import torch
+    import zealot_b200 as zb
+    torch.cuda.set_device(0)
+    ctx = zb.GpuContext(0)
+    attn = zb.CudaAttention(ctx)
+    stream = torch.cuda.Stream(0)
+    args.side_steps = args.steps
+    res = side_measurements(ctx, attn, stream, load_peaks(), args, only=args.workload)
+    key = "prefill" if args.workload == "prefill" else "reshape_and_cache"
+    r = res[key]
+    line = {"metric": "prefill_tflops" if key == "prefill" else "reshape_and_cache_gbs",
+            "value": r["tflops"] if key == "prefill" else r["gbs"],
+            "unit": "TFLOP/s" if key == "prefill" else "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "dtype": "bf16",
+            "config": {"workload": r["workload"]}, "detail": r}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -361,12 +394,13 @@ def load_peaks():
 
 
 def load_traffic(name):
-    p = os.path.join(ROOT, "profiles", f"{name}_traffic.json")
+    """DRAM bytes per launch (dram__bytes_read.sum + write.sum) from the committed ncu
+    summary of the same kernel on the same batch (profiles/<name>.md)."""
+    p = os.path.join(ROOT, "profiles", f"{name}.md")
     if os.path.exists(p):
-        try:
-            return json.load(open(p)).get("dram_bytes_per_launch")
-        except (OSError, ValueError):
-            return None
+        for line in open(p):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":")[1])
     return None
 
 
@@ -450,6 +484,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-side", action="store_true", help="skip the prefill / cache side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "prefill", "cache"], default="decode",
+                    help="decode (C2, the headline) or a single side kernel on its C3 workload")
+    ap.add_argument("--lite", action="store_true",
+                    help="only warm-up + timed steps of the kernel (no clock soak, e2e, side runs or "
+                         "CPU baseline): the form used under ncu")
+    ap.add_argument("--pool-blocks", type=int, default=NUM_BLOCKS,
+                    help="KV pool size in blocks per GPU; 0 = just the blocks the batch references")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -458,8 +499,13 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.gpus != world:
         log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; running {world} rank(s)")
+    if args.lite:
+        args.no_side = args.no_cpu_baseline = True
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload != "decode":
+        run_side_only(args)
         return
     run_ours(args, rank, world, local_rank)
 
