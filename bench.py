@@ -243,7 +243,8 @@ def run_ours(args, rank, world, local_rank):
     peaks = load_peaks()
     alg = algorithmic_bytes(lens, hkv_l, h_l)
     achieved = alg / (dev_ms / args.steps * 1e-3) / 1e9
-    traffic = load_traffic("decode_c2_paged_decode_bf16")
+    # the committed ncu capture is of the 1-GPU step; other N move different bytes
+    traffic = load_traffic("decode_c2_paged_decode_bf16") if world == 1 else None
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
             "algorithmic_bytes": alg, "peak_source": peaks["source"]}

@@ -1,0 +1,97 @@
+"""Multi-GPU partitioning of the attention path (one process per GPU).
+
+Two ways to spread the work, matching the north star of the path:
+
+* kv-head-group sharding (no collective): GPU r of N owns kv heads
+  [r*Hkv/N, (r+1)*Hkv/N) and their query heads; its pools hold only those
+  heads, and every GPU uses the same block ids and tables. Decode and prefill
+  outputs are complete heads, so nothing is exchanged.
+* sequence split (one sequence's KV spread over GPUs): GPU r attends to a
+  contiguous, block-aligned token range of each sequence and produces the
+  partial triple (m, l, o); the triples are all-gathered over NVLink with NCCL
+  and merged (zl_nccl_merge), since the merge is not a sum.
+
+The reference engine is single-device (`CudaModelRunner::load(id, 0)`,
+src/bin/zealot-backend.rs:317); this module has no counterpart there.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from .context import GpuContext, GQA_GROUPED, dtype_code, ptr
+from .errors import check, InvalidArgument
+
+
+def kv_head_group(rank: int, world: int, num_kv_heads: int) -> tuple[int, int]:
+    """[lo, hi) kv heads owned by `rank`; the kv heads must divide over the GPUs."""
+    if world <= 0 or not 0 <= rank < world:
+        raise InvalidArgument(f"rank {rank} of {world}")
+    if num_kv_heads % world:
+        raise InvalidArgument(f"{num_kv_heads} kv heads do not divide over {world} GPUs")
+    per = num_kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def query_heads_of(kv_lo: int, kv_hi: int, num_heads: int, num_kv_heads: int) -> tuple[int, int]:
+    """Query heads [lo, hi) served by kv heads [kv_lo, kv_hi) under the grouped mapping."""
+    g = num_heads // num_kv_heads
+    return kv_lo * g, kv_hi * g
+
+
+def token_split(seq_lens, rank: int, world: int, block_size: int):
+    """Block-aligned contiguous token range [begin, end) of every sequence for `rank`.
+
+    Each sequence's blocks are dealt out in contiguous runs of equal count (the
+    first ranks take one extra block when it does not divide), so a GPU only needs
+    the pool blocks of its own range.
+    """
+    lens = np.asarray(seq_lens, dtype=np.int64)
+    nblk = (lens + block_size - 1) // block_size
+    base, extra = nblk // world, nblk % world
+    b_lo = rank * base + np.minimum(rank, extra)
+    b_hi = b_lo + base + (rank < extra)
+    begin = np.minimum(b_lo * block_size, lens)
+    end = np.minimum(b_hi * block_size, lens)
+    return begin.astype(np.int32), end.astype(np.int32)
+
+
+class SequenceSplitDecoder:
+    """Decode for sequences whose KV is split across GPUs: local partial triples,
+    NCCL all-gather over NVLink, merge kernel. One instance per process/GPU."""
+
+    def __init__(self, ctx: GpuContext, rank: int, world: int, broadcast_id):
+        """`broadcast_id(bytes_or_None) -> bytes` shares rank 0's 128-byte NCCL id
+        (e.g. via torch.distributed.broadcast_object_list)."""
+        self.ctx, self.lib, self.rank, self.world = ctx, ctx.lib, rank, world
+        buf = (ctypes.c_uint8 * 128)()
+        if rank == 0:
+            check(self.lib.zl_nccl_get_unique_id(buf))
+            uid = broadcast_id(bytes(buf))
+        else:
+            uid = broadcast_id(None)
+        ctypes.memmove(buf, uid, 128)
+        check(self.lib.zl_nccl_init(ctx.handle, buf, world, rank))
+
+    def decode(self, q, k_pool, v_pool, block_tables, tok_begin, tok_end, out, num_heads: int,
+               num_kv_heads: int, head_dim: int, block_size: int, max_blocks_per_seq: int,
+               num_blocks: int | None = None, scale: float = 0.0, gqa_map: int = GQA_GROUPED,
+               stream=None) -> None:
+        import torch
+        B = tok_end.numel()
+        m = torch.empty((B, num_heads), dtype=torch.float32, device=q.device)
+        l = torch.empty_like(m)
+        o = torch.empty((B, num_heads, head_dim), dtype=torch.float32, device=q.device)
+        if num_blocks is None:
+            num_blocks = k_pool.numel() // (block_size * num_kv_heads * head_dim)
+        st = self.ctx.stream(stream)
+        check(self.lib.zl_paged_decode_partial(
+            self.ctx.handle, ptr(q), ptr(k_pool), ptr(v_pool), ptr(block_tables), ptr(tok_begin),
+            ptr(tok_end), ptr(m), ptr(l), ptr(o), B, num_heads, num_kv_heads, head_dim, block_size,
+            max_blocks_per_seq, num_blocks, scale, gqa_map, dtype_code(q.dtype), st))
+        check(self.lib.zl_nccl_merge(self.ctx.handle, ptr(m), ptr(l), ptr(o), B * num_heads,
+                                     head_dim, ptr(out), dtype_code(out.dtype), st))
+
+    def close(self) -> None:
+        check(self.lib.zl_nccl_finalize(self.ctx.handle))
