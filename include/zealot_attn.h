@@ -124,7 +124,7 @@ zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const 
  * device-wide synchronisation cudaMalloc/cudaFree imply. Same kernel and
  * results as zl_paged_decode for bf16, head_dim 128, block_size 16, grouped
  * GQA with <= 8 query heads per kv head; no zl_ctx, the current device is
- * used. Its split-KV scratch is a static device array of about 10.7 MB that
+ * used. Its split-KV scratch is a static device array of about 5.4 MB that
  * every GPU which loads the library holds until the process exits. Limits:
  * num_seqs <= 4096 and num_seqs * num_kv_heads <= 16384, else
  * ZL_ERR_INVALID_ARG; other shapes return ZL_ERR_UNSUPPORTED. The first call

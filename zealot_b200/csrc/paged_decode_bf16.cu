@@ -196,64 +196,86 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   int* winfo = info + warp * STAGES;
   const uint64_t policy = policy_evict_first();
 
-  // ---------------- producer state (lane 0 only) ----------------
-  int pb = 0, pkvh = 0, pj = 0;
-  bool ptrunc = false;
+  // ---------------- producer: block list in chunks of 32 (warp-wide) ----------------
+  // Every 32 blocks the whole warp resolves the next 32 entries of its range
+  // at once (one coalesced table read, one seq_lens read per lane): lane L
+  // holds the TMA row and valid-token count of block ch_base + L. A negative
+  // table entry ends its sequence (paged_attention.cu:66-67): a block is
+  // dropped when any entry at or before it in the same (sequence, kv head)
+  // is negative, tracked across chunks by carry_seg / carry_trunc.
+  const int32_t* const tables = a.block_tables;
+  int ch_base = -32, ch_y = 0, ch_nv = 0;
+  int carry_seg, carry_trunc;
   {
     int b, kvh, j;
     locate(f0, b, kvh, j);
-    pb = b; pkvh = kvh; pj = j;
-    // A negative entry before j (in a block another warp handles) ends the
-    // sequence for this warp too.
     bool neg = false;
-    const int32_t* tb = a.block_tables + (int64_t)b * a.max_blocks;
+    const int32_t* tb = tables + (int64_t)b * a.max_blocks;
     for (int t = lane; t < j; t += 32) neg |= (tb[t] < 0);
-    ptrunc = __any_sync(0xffffffffu, neg);
+    carry_trunc = __any_sync(0xffffffffu, neg) ? 1 : 0;
+    carry_seg = b * Hkv + kvh;
   }
-  auto produce = [&](int i) {
-    // called by lane 0 for the i-th block of this warp's range
-    const int slot = i % STAGES;
-    const int nb = prefix[pb + 1] - prefix[pb];
-    if (pj == 0) ptrunc = false;
-    const int32_t e = a.block_tables[(int64_t)pb * a.max_blocks + pj];
-    int nvalid = 0;
-    if (!ptrunc) {
-      if (e < 0) {
-        ptrunc = true;
-      } else if ((int64_t)e >= a.num_blocks) {
+  auto build_chunk = [&](int base) {
+    const int idx = base + lane;
+    const bool ok = idx < nwork;
+    int seg = -1, e = 0, b = 0, kvh = 0, j = 0;
+    if (ok) {
+      locate(f0 + idx, b, kvh, j);
+      seg = b * Hkv + kvh;
+      e = tables[(int64_t)b * a.max_blocks + j];
+    }
+    const unsigned negm = __ballot_sync(0xffffffffu, ok && e < 0);
+    const int prev = __shfl_up_sync(0xffffffffu, seg, 1);
+    const unsigned startm = __ballot_sync(0xffffffffu, lane == 0 || seg != prev);
+    const unsigned upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+    const int my_start = 31 - __clz(startm & upto);
+    bool trunc = (negm & upto & ~((1u << my_start) - 1u)) != 0;
+    if (my_start == 0 && seg == carry_seg && carry_trunc) trunc = true;
+    int nv = 0, y = 0;
+    if (ok && !trunc) {
+      if ((int64_t)e >= a.num_blocks) {
         atomicOr(a.status, ZL_DEV_OOB);
       } else {
-        const int len = a.seq_lens[pb];
-        nvalid = (pj == nb - 1) ? (len - pj * BS) : BS;
+        const int nb = prefix[b + 1] - prefix[b];
+        nv = (j == nb - 1) ? (a.seq_lens[b] - j * BS) : BS;
+        y = (int)(((int64_t)e * Hkv + kvh) * BS);
       }
     }
-    winfo[slot] = nvalid;
-    const uint32_t bar = smem_u32(&wbars[slot]);
-    if (nvalid > 0) {
-      const uint32_t dst = ring + slot * STAGE;
-      const int y = (int)(((int64_t)e * Hkv + pkvh) * BS);
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(bar, STAGE);
-      tma_load_2d_hint(dst, &tmK, 0, y, bar, policy);
-      tma_load_2d_hint(dst + 2048, &tmK, 64, y, bar, policy);
-      tma_load_2d_hint(dst + TILE, &tmV, 0, y, bar, policy);
-      tma_load_2d_hint(dst + TILE + 2048, &tmV, 64, y, bar, policy);
-    } else {
-      mbar_arrive(bar);
-    }
-    // advance (b, kvh, j)
-    if (++pj == nb) {
-      pj = 0;
-      if (++pkvh == Hkv) {
-        pkvh = 0;
-        do { pb++; } while (pb < B && prefix[pb + 1] == prefix[pb]);
+    const int last = min(31, nwork - 1 - base);
+    carry_seg = __shfl_sync(0xffffffffu, seg, last);
+    carry_trunc = __shfl_sync(0xffffffffu, trunc ? 1 : 0, last);
+    ch_base = base;
+    ch_y = y;
+    ch_nv = nv;
+  };
+  // Issue the loads of block i of this warp's range into its ring slot (all
+  // lanes call; lane 0 issues).
+  auto produce = [&](int i) {
+    if (i >= ch_base + 32) build_chunk(i & ~31);
+    const int src = i - ch_base;
+    const int y = __shfl_sync(0xffffffffu, ch_y, src);
+    const int nvalid = __shfl_sync(0xffffffffu, ch_nv, src);
+    if (lane == 0) {
+      const int slot = i % STAGES;
+      winfo[slot] = nvalid;
+      const uint32_t bar = smem_u32(&wbars[slot]);
+      if (nvalid > 0) {
+        const uint32_t dst = ring + slot * STAGE;
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, STAGE);
+        tma_load_2d_hint(dst, &tmK, 0, y, bar, policy);
+        tma_load_2d_hint(dst + 2048, &tmK, 64, y, bar, policy);
+        tma_load_2d_hint(dst + TILE, &tmV, 0, y, bar, policy);
+        tma_load_2d_hint(dst + TILE + 2048, &tmV, 64, y, bar, policy);
+      } else {
+        mbar_arrive(bar);
       }
     }
   };
 
-  if (lane == 0) {
+  {
     const int pre = min(nwork, STAGES);
-    for (int i = 0; i < pre; i++) produce(i);
+    for (int k = 0; k < pre; k++) produce(k);
   }
   __syncwarp();
 
@@ -263,6 +285,17 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   const int quad = lane >> 2;   // 0..7 : token row (S), head column (B operand)
   const int qid = lane & 3;     // 0..3
   const int mat = lane >> 3, mrow = lane & 7;
+  // this lane's ldmatrix row addresses inside a K / V tile (swizzled)
+  uint32_t kofs[8], vofs[8];
+#pragma unroll
+  for (int t = 0; t < 8; t++) {
+    kofs[t] = tile_off(mrow + ((mat & 1) << 3), 2 * t + (mat >> 1));
+    vofs[t] = tile_off(mrow + ((mat >> 1) << 3), 2 * t + (mat & 1));
+  }
+  // The running max only moves when a score exceeds it by more than 2^8: until
+  // then p = 2^(s - m) <= 256 stays exact enough in bf16 and fp32, and the
+  // block needs neither the max reduction nor the O rescale.
+  constexpr float kLazy = 8.f;
   bool timed_out = false;
 
   int i = 0;
@@ -273,7 +306,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     const int64_t seg_S = (int64_t)prefix[cb] * Hkv + (int64_t)ckvh * nb;
     const int64_t seg_E = seg_S + nb;
     const int64_t seg_rem = f1 - seg_S;
-    const int seg_jend = seg_rem < (int64_t)nb ? (int)seg_rem : nb;  // exclusive
+    const int seg_jend = seg_rem < (int64_t)nb ? (int)seg_rem : nb;
     const int G = a.G;
     const int head0 = ckvh * G;
 
@@ -314,40 +347,48 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
           }
           __syncwarp();
         }
-        // S^T[16 tok][8 heads] = K[16][128] * q^T
+        // S^T[16 tok][8 heads] = K[16][128] * q^T, two independent k chains
         float s[4] = {0.f, 0.f, 0.f, 0.f};
+        float s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-          uint32_t a0, a1, a2, a3;
-          const int r = mrow + ((mat & 1) << 3);
-          const int c = 2 * ks + (mat >> 1);
-          ldsm_x4(ks_base + tile_off(r, c), a0, a1, a2, a3);
+        for (int ks = 0; ks < 8; ks += 2) {
+          uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+          ldsm_x4(ks_base + kofs[ks], a0, a1, a2, a3);
+          ldsm_x4(ks_base + kofs[ks + 1], c0, c1, c2, c3);
           mma_bf16_16816(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+          mma_bf16_16816(s2, c0, c1, c2, c3, qf[ks + 1][0], qf[ks + 1][1]);
         }
         // mask + scale to log2 units
         const bool v0 = quad < nvalid, v1 = quad + 8 < nvalid;
-        s[0] = v0 ? s[0] * a.scale_log2 : -INFINITY;
-        s[1] = v0 ? s[1] * a.scale_log2 : -INFINITY;
-        s[2] = v1 ? s[2] * a.scale_log2 : -INFINITY;
-        s[3] = v1 ? s[3] * a.scale_log2 : -INFINITY;
-        float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
+        const float sc = a.scale_log2;
+        s[0] = v0 ? (s[0] + s2[0]) * sc : -INFINITY;
+        s[1] = v0 ? (s[1] + s2[1]) * sc : -INFINITY;
+        s[2] = v1 ? (s[2] + s2[2]) * sc : -INFINITY;
+        s[3] = v1 ? (s[3] + s2[3]) * sc : -INFINITY;
+        const bool grow = fmaxf(s[0], s[2]) > m0 + kLazy || fmaxf(s[1], s[3]) > m1 + kLazy;
+        if (__any_sync(0xffffffffu, grow)) {
+          float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
 #pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-          bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
-          bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
-        }
-        const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
-        const float al0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mn0);
-        const float al1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mn1);
-        m0 = mn0; m1 = mn1;
-        const float p0 = ex2(s[0] - mn0), p1 = ex2(s[1] - mn1);
-        const float p2 = ex2(s[2] - mn0), p3 = ex2(s[3] - mn1);
-        l0 = l0 * al0 + (p0 + p2);
-        l1 = l1 * al1 + (p1 + p3);
+          for (int off = 4; off < 32; off <<= 1) {
+            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+          }
+          const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+          const float al0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mn0);
+          const float al1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mn1);
+          m0 = mn0; m1 = mn1;
+          l0 *= al0; l1 *= al1;
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-          o[t][0] *= al0; o[t][1] *= al1; o[t][2] *= al0; o[t][3] *= al1;
+          for (int t = 0; t < 8; t++) {
+            o[t][0] *= al0; o[t][1] *= al1; o[t][2] *= al0; o[t][3] *= al1;
+          }
         }
+        const float p0 = s[0] == -INFINITY ? 0.f : ex2(s[0] - m0);
+        const float p1 = s[1] == -INFINITY ? 0.f : ex2(s[1] - m1);
+        const float p2 = s[2] == -INFINITY ? 0.f : ex2(s[2] - m0);
+        const float p3 = s[3] == -INFINITY ? 0.f : ex2(s[3] - m1);
+        l0 += p0 + p2;
+        l1 += p1 + p3;
         // P^T as the B operand: transpose the two 8x8 (tok x head) halves
         const uint32_t b0 = movm_t(pack_bf16x2(p0, p1));
         const uint32_t b1 = movm_t(pack_bf16x2(p2, p3));
@@ -355,20 +396,17 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
 #pragma unroll
         for (int t = 0; t < 8; t++) {
           uint32_t a0, a1, a2, a3;
-          const int r = mrow + ((mat >> 1) << 3);
-          const int c = 2 * t + (mat & 1);
-          ldsm_x4_t(vs_base + tile_off(r, c), a0, a1, a2, a3);
+          ldsm_x4_t(vs_base + vofs[t], a0, a1, a2, a3);
           mma_bf16_16816(o[t], a0, a1, a2, a3, b0, b1);
         }
       }
       __syncwarp();
-      if (lane == 0 && i + STAGES < nwork) produce(i + STAGES);
+      if (i + STAGES < nwork) produce(i + STAGES);
       __syncwarp();
     }
     if (timed_out) break;
 
     // ----- finish the segment
-    const int nb_cur = nb;
     float L0 = l0, L1 = l1;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
@@ -447,7 +485,6 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         if (lane == 0) a.counters[cidx] = 0;
       }
     }
-    (void)nb_cur;
     // advance consumer to the next segment
     cj = 0;
     if (++ckvh == Hkv) {
@@ -480,8 +517,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-constexpr int kWarps = 8;
-constexpr int kStages = 3;
+// Warps per CTA (one CTA per SM) and ring depth per warp. Measured on B200
+// (C2 step): one consumer warp per SM sub-partition is fastest -- 4 warps x 4
+// stages reach 85 % of the copy bandwidth, 8 x 3 only 72 %, 2 x 8 50 %.
+#ifndef ZL_DECODE_WARPS
+#define ZL_DECODE_WARPS 4
+#endif
+#ifndef ZL_DECODE_STAGES
+#define ZL_DECODE_STAGES 4
+#endif
+constexpr int kWarps = ZL_DECODE_WARPS;
+constexpr int kStages = ZL_DECODE_STAGES;
 
 }  // namespace
 
@@ -572,7 +618,7 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
 // the device-wide synchronisation cudaMalloc/cudaFree imply. For them,
 // zl_paged_decode_noalloc runs the same kernel with its scratch in the
 // file-scope array below, which is part of the loaded module: every GPU that
-// loads this library holds it (about 10.7 MB) until the process exits.
+// loads this library holds it (about 5.4 MB) until the process exits.
 //
 // Limits: bf16, head_dim 128, block_size 16, grouped GQA with at most 8
 // query heads per kv head, num_seqs <= 4096, num_seqs * num_kv_heads <=
