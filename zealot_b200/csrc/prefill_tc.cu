@@ -195,55 +195,86 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
     const int q_row = BM * t + r;              // row index within the sequence
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    // The running max only moves when a tile's row max exceeds it by more
+    // than 2^8: until then p = 2^(s - m) <= 256 is exact enough in bf16/fp32
+    // and the O rescale (a TMEM round trip of 128 columns) is skipped.
+    constexpr float kLazy = 8.f;
+    const float sc = a.scale_log2;
     for (int j = 0; j < nkv; j++) {
       if (!(ok = mbar_wait_warp(bar(S_FULL + w), j & 1, a.status))) break;
       tc_fence_after();
-      const int key0 = BN * j;
-      const bool edge = (j == nkv - 1);
-      // keys valid for this row: < key_lim
-      const int key_lim = edge ? (a.causal ? min(q_row + 1, L) : L) - key0 : BN;
-      uint32_t v[32];
+      // only the last tile of a row range needs a mask (the diagonal when causal)
+      const bool edge = (j == nkv - 1) && (a.causal || (L % BN) != 0);
+      const int key_lim = edge ? (a.causal ? min(q_row + 1, L) : L) - BN * j : BN;
+      uint32_t va[32], vb[32];
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        tmem_ld32(tSr + 32 * c, v);
+      for (int hh = 0; hh < 2; hh++) {  // two 32-column chunks per TMEM wait
+        tmem_ld32(tSr + 64 * hh, va);
+        tmem_ld32(tSr + 64 * hh + 32, vb);
         tc_wait_ld();
+        if (edge) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const float x = __uint_as_float(v[i]);
-          mx = (32 * c + i < key_lim) ? fmaxf(mx, x) : mx;
+          for (int i = 0; i < 32; i++) {
+            mx = (64 * hh + i < key_lim) ? fmaxf(mx, __uint_as_float(va[i])) : mx;
+            mx = (64 * hh + 32 + i < key_lim) ? fmaxf(mx, __uint_as_float(vb[i])) : mx;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i++) mx = fmaxf(mx, fmaxf(__uint_as_float(va[i]), __uint_as_float(vb[i])));
         }
       }
-      const float m_new = fmaxf(m, mx * a.scale_log2);
+      const float m_tile = mx * sc;
+      const bool grow = m_tile > m + kLazy;
+      const bool any_grow = __any_sync(0xffffffffu, grow);
+      const float m_new = grow ? fmaxf(m, m_tile) : m;
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_use);
       float lsum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        tmem_ld32(tSr + 32 * c, v);
+      for (int hh = 0; hh < 2; hh++) {
+        tmem_ld32(tSr + 64 * hh, va);
+        tmem_ld32(tSr + 64 * hh + 32, vb);
         tc_wait_ld();
-        uint32_t pk[16];
+        uint32_t pa[16], pb[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          const int k0 = 32 * c + 2 * i;
-          const float p0 = (k0 < key_lim) ? ex2(__uint_as_float(v[2 * i]) * a.scale_log2 - m_use) : 0.f;
-          const float p1 = (k0 + 1 < key_lim) ? ex2(__uint_as_float(v[2 * i + 1]) * a.scale_log2 - m_use) : 0.f;
-          lsum += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
+          const int k0 = 64 * hh + 2 * i, k1 = k0 + 32;
+          float p0 = ex2(__uint_as_float(va[2 * i]) * sc - m_use);
+          float p1 = ex2(__uint_as_float(va[2 * i + 1]) * sc - m_use);
+          float p2 = ex2(__uint_as_float(vb[2 * i]) * sc - m_use);
+          float p3 = ex2(__uint_as_float(vb[2 * i + 1]) * sc - m_use);
+          if (edge) {
+            p0 = k0 < key_lim ? p0 : 0.f;
+            p1 = k0 + 1 < key_lim ? p1 : 0.f;
+            p2 = k1 < key_lim ? p2 : 0.f;
+            p3 = k1 + 1 < key_lim ? p3 : 0.f;
+          }
+          lsum += (p0 + p1) + (p2 + p3);
+          pa[i] = pack_bf16x2(p0, p1);
+          pb[i] = pack_bf16x2(p2, p3);
         }
-        tmem_st16(tSr + 16 * c, pk);
+        // P over the first 64 columns of S: chunk c goes to columns [16c, 16c+16),
+        // all below the S columns still to be read
+        tmem_st16(tSr + 32 * hh, pa);
+        tmem_st16(tSr + 32 * hh + 16, pb);
       }
       l = l * alpha + lsum;
-      // tcgen05.ld/st are warp-collective: the rescale branch must be taken by
-      // the whole warp (rows whose max did not move multiply by alpha == 1).
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // tcgen05.ld/st are warp-collective: the rescale branch is taken by the
+      // whole warp (rows whose max did not move multiply by alpha == 1).
+      if (j > 0 && any_grow) {
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-          tmem_ld32(tOr + 32 * c, v);
+        for (int hh = 0; hh < 2; hh++) {
+          tmem_ld32(tOr + 64 * hh, va);
+          tmem_ld32(tOr + 64 * hh + 32, vb);
           tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          tmem_st32(tOr + 32 * c, v);
+          for (int i = 0; i < 32; i++) {
+            va[i] = __float_as_uint(__uint_as_float(va[i]) * alpha);
+            vb[i] = __float_as_uint(__uint_as_float(vb[i]) * alpha);
+          }
+          tmem_st32(tOr + 64 * hh, va);
+          tmem_st32(tOr + 64 * hh + 32, vb);
         }
       }
       m = m_new;
