@@ -327,47 +327,79 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
 #pragma unroll
     for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
 
-    for (int j = seg_j0; j < seg_jend; j++, i++) {
-      const int slot = i % STAGES;
-      const uint32_t bar = smem_u32(&wbars[slot]);
-      if (!mbar_wait_warp(bar, (uint32_t)((i / STAGES) & 1), a.status)) {
+    // Two 16-token blocks per step: their K/V tiles feed interleaved MMA
+    // chains and share one softmax / rescale decision. A step whose second
+    // block is missing (odd count) or skipped reads the valid block's tile for
+    // both with the missing one fully masked, so no unloaded tile is read.
+    for (int j = seg_j0; j < seg_jend;) {
+      const bool two = j + 1 < seg_jend;
+      const int slotA = i % STAGES;
+      if (!mbar_wait_warp(smem_u32(&wbars[slotA]), (uint32_t)((i / STAGES) & 1), a.status)) {
         timed_out = true;
         break;
       }
-      const int nvalid = winfo[slot];
-      const uint32_t ks_base = ring + slot * STAGE;
-      const uint32_t vs_base = ks_base + TILE;
-      if (nvalid > 0) {
-        if (nvalid < BS) {
-          // zero V rows past the context so 0 * garbage cannot be NaN
-          uint8_t* vt = base + (vs_base - base_u32);
-          for (int x = lane; x < (BS - nvalid) * 16; x += 32) {
-            const int r = nvalid + (x >> 4), c = x & 15;
+      int slotB = slotA, nvB = 0;
+      const int nvA = winfo[slotA];
+      if (two) {
+        slotB = (i + 1) % STAGES;
+        if (!mbar_wait_warp(smem_u32(&wbars[slotB]), (uint32_t)(((i + 1) / STAGES) & 1), a.status)) {
+          timed_out = true;
+          break;
+        }
+        nvB = winfo[slotB];
+      }
+      if (nvA > 0 || nvB > 0) {
+        uint32_t kA = ring + slotA * STAGE, kB = ring + slotB * STAGE;
+        if (nvA == 0) kA = kB;
+        if (nvB == 0) kB = kA;
+        // zero V rows past the context so 0 * garbage cannot be NaN
+        if (nvA > 0 && nvA < BS) {
+          uint8_t* vt = base + (kA + TILE - base_u32);
+          for (int x = lane; x < (BS - nvA) * 16; x += 32) {
+            const int r = nvA + (x >> 4), c = x & 15;
             *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
           }
-          __syncwarp();
         }
-        // S^T[16 tok][8 heads] = K[16][128] * q^T, two independent k chains
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        float s2[4] = {0.f, 0.f, 0.f, 0.f};
+        if (nvB > 0 && nvB < BS) {
+          uint8_t* vt = base + (kB + TILE - base_u32);
+          for (int x = lane; x < (BS - nvB) * 16; x += 32) {
+            const int r = nvB + (x >> 4), c = x & 15;
+            *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        __syncwarp();
+        // S^T = K q^T for both blocks, four independent chains
+        float sA[4] = {0.f, 0.f, 0.f, 0.f}, sA2[4] = {0.f, 0.f, 0.f, 0.f};
+        float sB[4] = {0.f, 0.f, 0.f, 0.f}, sB2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < 8; ks += 2) {
-          uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
-          ldsm_x4(ks_base + kofs[ks], a0, a1, a2, a3);
-          ldsm_x4(ks_base + kofs[ks + 1], c0, c1, c2, c3);
-          mma_bf16_16816(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
-          mma_bf16_16816(s2, c0, c1, c2, c3, qf[ks + 1][0], qf[ks + 1][1]);
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3, d0, d1, d2, d3;
+          ldsm_x4(kA + kofs[ks], a0, a1, a2, a3);
+          ldsm_x4(kB + kofs[ks], b0, b1, b2, b3);
+          ldsm_x4(kA + kofs[ks + 1], c0, c1, c2, c3);
+          ldsm_x4(kB + kofs[ks + 1], d0, d1, d2, d3);
+          mma_bf16_16816(sA, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+          mma_bf16_16816(sB, b0, b1, b2, b3, qf[ks][0], qf[ks][1]);
+          mma_bf16_16816(sA2, c0, c1, c2, c3, qf[ks + 1][0], qf[ks + 1][1]);
+          mma_bf16_16816(sB2, d0, d1, d2, d3, qf[ks + 1][0], qf[ks + 1][1]);
         }
         // mask + scale to log2 units
-        const bool v0 = quad < nvalid, v1 = quad + 8 < nvalid;
         const float sc = a.scale_log2;
-        s[0] = v0 ? (s[0] + s2[0]) * sc : -INFINITY;
-        s[1] = v0 ? (s[1] + s2[1]) * sc : -INFINITY;
-        s[2] = v1 ? (s[2] + s2[2]) * sc : -INFINITY;
-        s[3] = v1 ? (s[3] + s2[3]) * sc : -INFINITY;
-        const bool grow = fmaxf(s[0], s[2]) > m0 + kLazy || fmaxf(s[1], s[3]) > m1 + kLazy;
+        const bool va0 = quad < nvA, va1 = quad + 8 < nvA;
+        const bool vb0 = quad < nvB, vb1 = quad + 8 < nvB;
+        sA[0] = va0 ? (sA[0] + sA2[0]) * sc : -INFINITY;
+        sA[1] = va0 ? (sA[1] + sA2[1]) * sc : -INFINITY;
+        sA[2] = va1 ? (sA[2] + sA2[2]) * sc : -INFINITY;
+        sA[3] = va1 ? (sA[3] + sA2[3]) * sc : -INFINITY;
+        sB[0] = vb0 ? (sB[0] + sB2[0]) * sc : -INFINITY;
+        sB[1] = vb0 ? (sB[1] + sB2[1]) * sc : -INFINITY;
+        sB[2] = vb1 ? (sB[2] + sB2[2]) * sc : -INFINITY;
+        sB[3] = vb1 ? (sB[3] + sB2[3]) * sc : -INFINITY;
+        const float c0m = fmaxf(fmaxf(sA[0], sA[2]), fmaxf(sB[0], sB[2]));
+        const float c1m = fmaxf(fmaxf(sA[1], sA[3]), fmaxf(sB[1], sB[3]));
+        const bool grow = c0m > m0 + kLazy || c1m > m1 + kLazy;
         if (__any_sync(0xffffffffu, grow)) {
-          float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
+          float bm0 = c0m, bm1 = c1m;
 #pragma unroll
           for (int off = 4; off < 32; off <<= 1) {
             bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
@@ -383,26 +415,38 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
             o[t][0] *= al0; o[t][1] *= al1; o[t][2] *= al0; o[t][3] *= al1;
           }
         }
-        const float p0 = s[0] == -INFINITY ? 0.f : ex2(s[0] - m0);
-        const float p1 = s[1] == -INFINITY ? 0.f : ex2(s[1] - m1);
-        const float p2 = s[2] == -INFINITY ? 0.f : ex2(s[2] - m0);
-        const float p3 = s[3] == -INFINITY ? 0.f : ex2(s[3] - m1);
-        l0 += p0 + p2;
-        l1 += p1 + p3;
-        // P^T as the B operand: transpose the two 8x8 (tok x head) halves
-        const uint32_t b0 = movm_t(pack_bf16x2(p0, p1));
-        const uint32_t b1 = movm_t(pack_bf16x2(p2, p3));
-        // O^T[128 d][8 heads] += V^T * P^T
+        float pA[4], pB[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const float mr = (r & 1) ? m1 : m0;
+          pA[r] = sA[r] == -INFINITY ? 0.f : ex2(sA[r] - mr);
+          pB[r] = sB[r] == -INFINITY ? 0.f : ex2(sB[r] - mr);
+        }
+        l0 += (pA[0] + pA[2]) + (pB[0] + pB[2]);
+        l1 += (pA[1] + pA[3]) + (pB[1] + pB[3]);
+        // P^T as the B operand: transpose the (tok x head) halves
+        const uint32_t ba0 = movm_t(pack_bf16x2(pA[0], pA[1]));
+        const uint32_t ba1 = movm_t(pack_bf16x2(pA[2], pA[3]));
+        const uint32_t bb0 = movm_t(pack_bf16x2(pB[0], pB[1]));
+        const uint32_t bb1 = movm_t(pack_bf16x2(pB[2], pB[3]));
+        // O^T[128 d][8 heads] += V_A^T P_A^T + V_B^T P_B^T
+        const uint32_t vA = kA + TILE, vB = kB + TILE;
 #pragma unroll
         for (int t = 0; t < 8; t++) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(vs_base + vofs[t], a0, a1, a2, a3);
-          mma_bf16_16816(o[t], a0, a1, a2, a3, b0, b1);
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+          ldsm_x4_t(vA + vofs[t], a0, a1, a2, a3);
+          ldsm_x4_t(vB + vofs[t], b0, b1, b2, b3);
+          mma_bf16_16816(o[t], a0, a1, a2, a3, ba0, ba1);
+          mma_bf16_16816(o[t], b0, b1, b2, b3, bb0, bb1);
         }
       }
       __syncwarp();
       if (i + STAGES < nwork) produce(i + STAGES);
+      if (two && i + 1 + STAGES < nwork) produce(i + 1 + STAGES);
       __syncwarp();
+      const int step = two ? 2 : 1;
+      i += step;
+      j += step;
     }
     if (timed_out) break;
 
@@ -518,13 +562,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Warps per CTA (one CTA per SM) and ring depth per warp. Measured on B200
-// (C2 step): one consumer warp per SM sub-partition is fastest -- 4 warps x 4
-// stages reach 85 % of the copy bandwidth, 8 x 3 only 72 %, 2 x 8 50 %.
+// (C2 step): one consumer warp per SM sub-partition is fastest -- 4 warps
+// reach 86 % of the copy bandwidth (4, 5 or 6 stages alike), 8 warps x 3
+// stages only 72 %, 3 warps 74 %, 2 warps 52 %.
 #ifndef ZL_DECODE_WARPS
 #define ZL_DECODE_WARPS 4
 #endif
 #ifndef ZL_DECODE_STAGES
-#define ZL_DECODE_STAGES 4
+#define ZL_DECODE_STAGES 6
 #endif
 constexpr int kWarps = ZL_DECODE_WARPS;
 constexpr int kStages = ZL_DECODE_STAGES;
