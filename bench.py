@@ -39,6 +39,16 @@ B_PER_GPU, H, HKV, D, BS, NUM_BLOCKS, MAX_BLOCKS = 64, 32, 8, 128, 16, 65536, 25
 CTX_LO, CTX_HI = 512, 4096
 SEED = 2024
 
+# Decode workloads. C2 (headline): Llama-3-8B layer, 64 sequences per GPU, weak
+# scaling over kv-head groups. C5: Llama-3-70B attention, 8 sequences of
+# 131072 tokens, the fixed job's kv-head groups sharded over the GPUs (strong).
+DECODE_SHAPES = {
+    "decode": dict(name="C2", b_per_gpu=64, b_total=None, H=32, HKV=8, ctx=(512, 4096), max_blocks=256,
+                   scaling="weak"),
+    "c5": dict(name="C5", b_per_gpu=None, b_total=8, H=64, HKV=8, ctx=(131072, 131072), max_blocks=8192,
+               scaling="strong"),
+}
+
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
@@ -46,16 +56,18 @@ def log(*a):
 
 # ------------------------------------------------------------------ workload
 
-def make_lens_tables(world: int, pool_blocks: int = NUM_BLOCKS):
+def make_lens_tables(world: int, pool_blocks: int = NUM_BLOCKS, shape=None):
     """Context lengths and block tables of the global batch (identical on every rank)."""
+    shape = shape or DECODE_SHAPES["decode"]
     rng = np.random.default_rng(SEED)
-    B = B_PER_GPU * world
-    lens = rng.integers(CTX_LO, CTX_HI + 1, size=B).astype(np.int32)
+    B = shape["b_total"] or shape["b_per_gpu"] * world
+    lo, hi = shape["ctx"]
+    lens = rng.integers(lo, hi + 1, size=B).astype(np.int32)
     nblk = (lens + BS - 1) // BS
     # per rank the pool holds its own kv heads' blocks; the tables index it
     pool_blocks = max(pool_blocks, int(nblk.sum()))
     perm = rng.permutation(pool_blocks).astype(np.int32)
-    tables = np.full((B, MAX_BLOCKS), -1, np.int32)
+    tables = np.full((B, shape["max_blocks"]), -1, np.int32)
     off = 0
     for b in range(B):
         tables[b, : nblk[b]] = perm[off: off + nblk[b]]
@@ -139,10 +151,12 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", dev))
 
-    lens, tables, pool_blocks = make_lens_tables(world, args.pool_blocks)
+    shape = DECODE_SHAPES[args.workload]
+    Hq, Hk, MAXB = shape["H"], shape["HKV"], shape["max_blocks"]
+    lens, tables, pool_blocks = make_lens_tables(world, args.pool_blocks, shape)
     B = len(lens)
-    hkv_l, h_l = HKV // world, H // world  # this rank's kv-head group
-    assert HKV % world == 0, "kv heads must divide over the GPUs"
+    hkv_l, h_l = Hk // world, Hq // world  # this rank's kv-head group
+    assert Hk % world == 0, "kv heads must divide over the GPUs"
     ctx = zb.GpuContext(dev)
     attn = zb.CudaAttention(ctx)
     stream = torch.cuda.Stream(dev)
@@ -158,7 +172,7 @@ def run_ours(args, rank, world, local_rank):
     s_handle = stream.cuda_stream
 
     def step():
-        attn.paged_forward(q, kpool, vpool, t_tab, t_len, out, B, h_l, hkv_l, D, BS, MAX_BLOCKS,
+        attn.paged_forward(q, kpool, vpool, t_tab, t_len, out, B, h_l, hkv_l, D, BS, MAXB,
                            num_blocks=pool_blocks, stream=s_handle)
 
     def barrier():
@@ -239,7 +253,7 @@ def run_ours(args, rank, world, local_rank):
         stream.wait_event(ev_in[b])
         base = d_in[b].data_ptr()
         rc = lib.zl_paged_decode(ctx.handle, base, ptr(kpool), ptr(vpool), base + off_tab, base + off_len,
-                                 ptr(d_out[b]), B, h_l, hkv_l, D, BS, MAX_BLOCKS, pool_blocks, 0.0, 0, 0, 1,
+                                 ptr(d_out[b]), B, h_l, hkv_l, D, BS, MAXB, pool_blocks, 0.0, 0, 0, 1,
                                  s_handle)
         assert rc == 0
         ev_done[b].record(stream)
@@ -270,7 +284,8 @@ def run_ours(args, rank, world, local_rank):
     alg = algorithmic_bytes(lens, hkv_l, h_l)
     achieved = alg / (dev_ms / args.steps * 1e-3) / 1e9
     # the committed ncu capture is of the 1-GPU step; other N move different bytes
-    traffic = load_traffic("decode_c2_paged_decode_bf16") if world == 1 else None
+    traffic = (load_traffic("decode_c2_paged_decode_bf16")
+               if world == 1 and args.workload == "decode" else None)
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
             "algorithmic_bytes": alg, "peak_source": peaks["source"]}
@@ -285,6 +300,20 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     if rank == 0:
         tokens_per_s = B / (ms_step * 1e-3)
+        if args.workload == "c5":
+            cfg = {"workload": "C5 long-context decode, Llama-3-70B attention shape: 64 q / 8 kv heads, head_dim 128, "
+                               "bf16, 8 sequences x 131072 tokens, block_size 16",
+                   "global_batch": B, "seq_len": 131072,
+                   "parallelism": f"kv-head groups x{world} of the fixed job (rank r: kv heads "
+                                  f"[r*{Hk // world}, (r+1)*{Hk // world})), split-KV inside each GPU",
+                   "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"}
+        else:
+            cfg = {"workload": "C2 paged decode, Llama-3-8B layer shape: 32 q / 8 kv heads, head_dim 128, "
+                               "bf16, block_size 16, 65536-block pool per GPU",
+                   "global_batch": B, "per_gpu_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                   "parallelism": f"kv-head groups x{world} (rank r: kv heads [r*{HKV // world}, "
+                                  f"(r+1)*{HKV // world}))",
+                   "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"}
         line = {
             "metric": "paged_decode_tokens_per_s",
             "value": round(tokens_per_s, 1),
@@ -294,16 +323,11 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup,
             "ms_per_step": round(ms_step, 5),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": shape["scaling"],
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) q/K/V, U[512,4096] contexts, random-permutation block tables)",
-            "config": {"workload": "C2 paged decode, Llama-3-8B layer shape: 32 q / 8 kv heads, head_dim 128, "
-                                   "bf16, block_size 16, 65536-block pool per GPU",
-                       "global_batch": B, "per_gpu_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
-                       "parallelism": f"kv-head groups x{world} (rank r: kv heads [r*{HKV // world}, "
-                                      f"(r+1)*{HKV // world}))",
-                       "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"},
+            "data": "synthetic (seeded N(0,1) q/K/V, random-permutation block tables)",
+            "config": cfg,
             "hbm_gbs": round(achieved, 1),
             "hbm_frac": round(achieved / peaks["hbm_gbs"], 4),
             "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
@@ -318,7 +342,7 @@ def run_ours(args, rank, world, local_rank):
         if args.lite:
             line["e2e"] = None
         line.update(side)
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.workload == "decode":
             line["cpu_baseline"] = cpu_baseline_single(lens, tables)
         print(json.dumps(line), flush=True)
     ctx.close()
@@ -512,8 +536,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-side", action="store_true", help="skip the prefill / cache side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "prefill", "cache"], default="decode",
-                    help="decode (C2, the headline) or a single side kernel on its C3 workload")
+    ap.add_argument("--workload", choices=["decode", "c5", "prefill", "cache"], default="decode",
+                    help="decode (C2, the headline), c5 (long-context decode), or a single side kernel "
+                         "on its C3 workload")
     ap.add_argument("--lite", action="store_true",
                     help="only warm-up + timed steps of the kernel (no clock soak, e2e, side runs or "
                          "CPU baseline): the form used under ncu")
@@ -532,9 +557,11 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    if args.workload != "decode":
+    if args.workload in ("prefill", "cache"):
         run_side_only(args)
         return
+    if args.workload == "c5":
+        args.no_side = True
     run_ours(args, rank, world, local_rank)
 
 

@@ -180,3 +180,33 @@ def test_partial_and_merge(ctx, oracle):
     ctx.check_status()
     full = oracle.paged_decode(q32, k32, v32, table, lens, H, Hkv, d, bs, kp.shape[0])
     assert rel_err(out.cpu().numpy(), full) <= 1e-4
+
+
+def test_bf16_c5_long_context(ctx, oracle):
+    """Config C5: 64 q / 8 kv heads, 8 sequences x 131072 tokens, 65536-block pool. All heads
+    run on the GPU; kv head group 3 (query heads 24-31) of every sequence is checked against
+    the oracle (a one-group slice of the pool keeps the host copy at 0.5 GB)."""
+    import torch
+    import zealot_b200 as zb
+    rng = np.random.default_rng(131072)
+    B, H, Hkv, d, bs, nb, L = 8, 64, 8, 128, 16, 65536, 131072
+    nblk = L // bs
+    perm = rng.permutation(nb).astype(np.int32)
+    table = perm.reshape(B, nblk).copy()
+    lens = np.full(B, L, np.int32)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    tk = torch.randn((nb, Hkv, bs, d), generator=g, device="cuda").to(torch.bfloat16)
+    tv = torch.randn((nb, Hkv, bs, d), generator=g, device="cuda").to(torch.bfloat16)
+    tq = torch.randn((B, H, d), generator=g, device="cuda").to(torch.bfloat16)
+    out = torch.full_like(tq, float("nan"))
+    zb.CudaAttention(ctx).paged_forward(tq, tk, tv, torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(),
+                                        out, B, H, Hkv, d, bs, nblk, num_blocks=nb)
+    ctx.check_status()
+    kvh = 3
+    k32 = tk[:, kvh:kvh + 1].float().cpu().numpy()
+    v32 = tv[:, kvh:kvh + 1].float().cpu().numpy()
+    q32 = tq[:, 8 * kvh: 8 * kvh + 8].float().cpu().numpy()
+    ref = oracle.paged_decode(q32, k32, v32, table, lens, 8, 1, d, bs, nb, num_threads=8)
+    got = out[:, 8 * kvh: 8 * kvh + 8].float().cpu().numpy()
+    assert not np.isnan(out.float().cpu().numpy()).any()
+    assert np.max(np.abs(got - ref)) <= BF16_ATOL
