@@ -207,7 +207,11 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
       const bool edge = (j == nkv - 1) && (a.causal || (L % BN) != 0);
       const int key_lim = edge ? (a.causal ? min(q_row + 1, L) : L) - BN * j : BN;
       uint32_t va[32], vb[32];
-      float mx = -INFINITY;
+      // 8 independent max accumulators: a 128-long dependent fmax chain would
+      // dominate the row's latency
+      float mx8[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) mx8[u] = -INFINITY;
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {  // two 32-column chunks per TMEM wait
         tmem_ld32(tSr + 64 * hh, va);
@@ -216,21 +220,27 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         if (edge) {
 #pragma unroll
           for (int i = 0; i < 32; i++) {
-            mx = (64 * hh + i < key_lim) ? fmaxf(mx, __uint_as_float(va[i])) : mx;
-            mx = (64 * hh + 32 + i < key_lim) ? fmaxf(mx, __uint_as_float(vb[i])) : mx;
+            const float xa = (64 * hh + i < key_lim) ? __uint_as_float(va[i]) : -INFINITY;
+            const float xb = (64 * hh + 32 + i < key_lim) ? __uint_as_float(vb[i]) : -INFINITY;
+            mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(xa, xb));
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; i++) mx = fmaxf(mx, fmaxf(__uint_as_float(va[i]), __uint_as_float(vb[i])));
+          for (int i = 0; i < 32; i++)
+            mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(__uint_as_float(va[i]), __uint_as_float(vb[i])));
         }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_tile = mx * sc;
       const bool grow = m_tile > m + kLazy;
       const bool any_grow = __any_sync(0xffffffffu, grow);
       const float m_new = grow ? fmaxf(m, m_tile) : m;
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_use);
-      float lsum = 0.f;
+      float ls8[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) ls8[u] = 0.f;
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {
         tmem_ld32(tSr + 64 * hh, va);
@@ -250,7 +260,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
             p2 = k1 < key_lim ? p2 : 0.f;
             p3 = k1 + 1 < key_lim ? p3 : 0.f;
           }
-          lsum += (p0 + p1) + (p2 + p3);
+          ls8[i & 7] += (p0 + p1) + (p2 + p3);
           pa[i] = pack_bf16x2(p0, p1);
           pb[i] = pack_bf16x2(p2, p3);
         }
@@ -259,6 +269,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         tmem_st16(tSr + 32 * hh, pa);
         tmem_st16(tSr + 32 * hh + 16, pb);
       }
+      const float lsum = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       l = l * alpha + lsum;
       // tcgen05.ld/st are warp-collective: the rescale branch is taken by the
       // whole warp (rows whose max did not move multiply by alpha == 1).
