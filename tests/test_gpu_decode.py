@@ -210,3 +210,28 @@ def test_bf16_c5_long_context(ctx, oracle):
     got = out[:, 8 * kvh: 8 * kvh + 8].float().cpu().numpy()
     assert not np.isnan(out.float().cpu().numpy()).any()
     assert np.max(np.abs(got - ref)) <= BF16_ATOL
+
+
+def test_bf16_one_kv_head_long_split(ctx, oracle):
+    """One GPU's shard of C5 at 8 GPUs: a single kv head (8 query heads) over 131072-token
+    sequences, so each sequence's stream splits over ~300 warps and the merge combines
+    hundreds of partial triples."""
+    import torch
+    import zealot_b200 as zb
+    rng = np.random.default_rng(77)
+    B, H, Hkv, d, bs, L = 2, 8, 1, 128, 16, 131072
+    nblk = L // bs
+    nb = B * nblk
+    table = rng.permutation(nb).astype(np.int32).reshape(B, nblk)
+    lens = np.array([L, L - 5], np.int32)
+    g = torch.Generator(device="cuda").manual_seed(77)
+    tk = torch.randn((nb, Hkv, bs, d), generator=g, device="cuda").to(torch.bfloat16)
+    tv = torch.randn((nb, Hkv, bs, d), generator=g, device="cuda").to(torch.bfloat16)
+    tq = torch.randn((B, H, d), generator=g, device="cuda").to(torch.bfloat16)
+    out = torch.full_like(tq, float("nan"))
+    zb.CudaAttention(ctx).paged_forward(tq, tk, tv, torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(),
+                                        out, B, H, Hkv, d, bs, nblk, num_blocks=nb)
+    ctx.check_status()
+    ref = oracle.paged_decode(tq.float().cpu().numpy(), tk.float().cpu().numpy(), tv.float().cpu().numpy(),
+                              table, lens, H, Hkv, d, bs, nb, num_threads=8)
+    assert np.max(np.abs(out.float().cpu().numpy() - ref)) <= BF16_ATOL

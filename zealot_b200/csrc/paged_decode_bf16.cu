@@ -497,34 +497,90 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       old = __shfl_sync(0xffffffffu, old, 0);
       if (old == ncontrib - 1) {
         __threadfence();
-        // merge all contributors of this (sequence, kv head)
-        for (int n = 0; n < G; n++) {
-          float M = -INFINITY;
-          for (int c = wa; c <= wb; c++) {
-            const int64_t fc = (int64_t)c * TB / W;
-            const int ec = (c == wa && fc < seg_S) ? 1 : 0;
-            M = fmaxf(M, __ldcg(&a.partials[2 * c + ec].m[n]));
+        // merge all contributors of this (sequence, kv head); lanes work on
+        // different contributors so the L2 reads overlap (long contexts split
+        // one sequence over dozens of warps)
+        const int nc = ncontrib;
+        auto slot_of = [&](int c) -> const Partial* {
+          const int64_t fc = (int64_t)c * TB / W;
+          return a.partials + 2 * c + ((c == wa && fc < seg_S) ? 1 : 0);
+        };
+        // (1) per-head max and weights: lane i handles contributors i, i+32, ...
+        float M[MAX_G], den[MAX_G];
+#pragma unroll
+        for (int n = 0; n < MAX_G; n++) { M[n] = -INFINITY; den[n] = 0.f; }
+        for (int c0 = 0; c0 < nc; c0 += 32)
+          if (c0 + lane < nc) {
+            const Partial* pc = slot_of(wa + c0 + lane);
+#pragma unroll
+            for (int n = 0; n < MAX_G; n++)
+              if (n < G) M[n] = fmaxf(M[n], __ldcg(&pc->m[n]));
           }
-          float den = 0.f;
-          float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int c = wa; c <= wb; c++) {
-            const int64_t fc = (int64_t)c * TB / W;
-            const int ec = (c == wa && fc < seg_S) ? 1 : 0;
-            const Partial* pc = a.partials + 2 * c + ec;
-            const float mc = __ldcg(&pc->m[n]);
-            if (mc == -INFINITY) continue;
-            const float w = __expf(mc - M);
-            den += w * __ldcg(&pc->l[n]);
-            const float4 oc = __ldcg(reinterpret_cast<const float4*>(&pc->o[n][0]) + lane);
-            num.x += w * oc.x; num.y += w * oc.y; num.z += w * oc.z; num.w += w * oc.w;
+#pragma unroll
+        for (int n = 0; n < MAX_G; n++)
+#pragma unroll
+          for (int off = 16; off; off >>= 1) M[n] = fmaxf(M[n], __shfl_xor_sync(0xffffffffu, M[n], off));
+        // (2) weighted sum of the o rows: every contributor's rows of all heads
+        // are loaded together (independent L2 reads), two contributors at a time
+        float4 num[MAX_G];
+#pragma unroll
+        for (int n = 0; n < MAX_G; n++) num[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c0 = 0; c0 < nc; c0 += 32) {
+          float wl[MAX_G];
+          if (c0 + lane < nc) {
+            const Partial* pc = slot_of(wa + c0 + lane);
+#pragma unroll
+            for (int n = 0; n < MAX_G; n++) {
+              wl[n] = 0.f;
+              if (n < G) {
+                const float mc = __ldcg(&pc->m[n]);
+                wl[n] = (mc == -INFINITY) ? 0.f : __expf(mc - M[n]);
+                den[n] += wl[n] * __ldcg(&pc->l[n]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int n = 0; n < MAX_G; n++) wl[n] = 0.f;
           }
-          const float inv = den > 0.f ? 1.f / den : 0.f;
-          __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
-          __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
-          uint2 pk;
-          pk.x = *reinterpret_cast<uint32_t*>(&lo);
-          pk.y = *reinterpret_cast<uint32_t*>(&hi);
-          reinterpret_cast<uint2*>(a.out + ((int64_t)cb * a.H + head0 + n) * D)[lane] = pk;
+          const int cnt = min(32, nc - c0);
+          for (int k = 0; k < cnt; k += 2) {
+            const bool second = k + 1 < cnt;
+            const float4* o1 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k)->o[0][0]) + lane;
+            const float4* o2 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k + (second ? 1 : 0))->o[0][0]) + lane;
+            float4 x1[MAX_G], x2[MAX_G];
+#pragma unroll
+            for (int n = 0; n < MAX_G; n++) {
+              if (n < G) {
+                x1[n] = __ldcg(o1 + n * (D / 4));
+                x2[n] = __ldcg(o2 + n * (D / 4));
+              }
+            }
+#pragma unroll
+            for (int n = 0; n < MAX_G; n++) {
+              const float w1 = __shfl_sync(0xffffffffu, wl[n], k);
+              const float w2 = second ? __shfl_sync(0xffffffffu, wl[n], k + 1) : 0.f;
+              if (n < G) {
+                num[n].x += w1 * x1[n].x + w2 * x2[n].x;
+                num[n].y += w1 * x1[n].y + w2 * x2[n].y;
+                num[n].z += w1 * x1[n].z + w2 * x2[n].z;
+                num[n].w += w1 * x1[n].w + w2 * x2[n].w;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < MAX_G; n++) {
+#pragma unroll
+          for (int off = 16; off; off >>= 1) den[n] += __shfl_xor_sync(0xffffffffu, den[n], off);
+          if (n < G) {
+            const float inv = den[n] > 0.f ? 1.f / den[n] : 0.f;
+            __nv_bfloat162 lo = __floats2bfloat162_rn(num[n].x * inv, num[n].y * inv);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(num[n].z * inv, num[n].w * inv);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(a.out + ((int64_t)cb * a.H + head0 + n) * D)[lane] = pk;
+          }
         }
         if (lane == 0) a.counters[cidx] = 0;
       }
