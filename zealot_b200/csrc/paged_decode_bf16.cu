@@ -54,7 +54,8 @@ struct DecodeArgs {
   const int32_t* seq_lens;     // [B]
   __nv_bfloat16* out;          // [B][H][D]
   Partial* partials;           // [2*W]
-  int* counters;               // [B*Hkv], zero on entry, zero on exit
+  int* counters;               // [0..1] grid barrier words, [2 + b*Hkv + kvh] merge counters;
+                               // all zero on entry and exit except the barrier generation
   int* status;
   int B, H, Hkv, G, max_blocks;
   int64_t num_blocks;
@@ -76,10 +77,50 @@ __device__ __forceinline__ uint32_t tile_off(int r, int c) {
   return (uint32_t)((c >> 3) * 2048 + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
 }
 
+// A split (sequence, kv head) with more contributor warps than this is merged
+// after a grid barrier by several warps instead of by its last contributor.
+constexpr int kMaxLastArriver = 16;
+
 // Warp index owning flat block x when TB blocks are split over W warps as
 // [gw*TB/W, (gw+1)*TB/W).
 __device__ __forceinline__ int owner_warp(int64_t x, int64_t TB, int64_t W) {
   return (int)(((x + 1) * W - 1) / TB);
+}
+
+// Grid-wide barrier of a cooperative launch (all CTAs co-resident). words[0]
+// counts arrivals and is reset by the last CTA, which then bumps words[1]
+// (the generation) that the others wait on. The wait is bounded and gives up
+// when another CTA has reported a timeout.
+__device__ bool grid_barrier(int* words, int* status) {
+  __shared__ int ok_s;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    volatile int* gen = words + 1;
+    const int g = *gen;
+    __threadfence();
+    int ok = 1;
+    if (atomicAdd(words, 1) + 1 == (int)gridDim.x) {
+      atomicExch(words, 0);
+      __threadfence();
+      atomicAdd(words + 1, 1);
+    } else {
+      const long long t0 = clock64();
+      while (*gen == g) {
+        __nanosleep(64);
+        if (aborted(status)) { ok = 0; break; }
+        if (clock64() - t0 > kWaitCycles) {
+          atomicOr(status, 2 /* ZL_DEV_TIMEOUT */);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    ok_s = ok;
+  }
+  __syncthreads();
+  return ok_s != 0;
 }
 
 template <int WARPS, int STAGES>
@@ -106,13 +147,16 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     prefetch_tmap(&tmV);
   }
   for (int i = tid; i < WARPS * STAGES; i += blockDim.x) mbar_init(smem_u32(&bars[i]), 1);
+  __shared__ int s_max_nb;  // longest sequence in blocks
+  if (tid == 0) s_max_nb = 0;
+  __syncthreads();
 
   // ---- per-CTA prologue: prefix[b] = Hkv * sum_{b'<b} nblk(b') (flat start of b)
   {
     constexpr int T = WARPS * 32;
     const int per = (B + T - 1) / T;
     const int b0 = tid * per;
-    int local = 0;
+    int local = 0, lmax = 0;
     for (int k = 0; k < per; k++) {
       const int b = b0 + k;
       if (b < B) {
@@ -123,15 +167,17 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
           nb = a.max_blocks;
         }
         local += nb;
+        lmax = max(lmax, nb);
       }
     }
+    if (lmax > 0) atomicMax(&s_max_nb, lmax);
     // block-wide exclusive scan of `local`
     int incl = local;
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
-    __shared__ int warp_tot[WARPS];
+    __shared__ int warp_tot[WARPS];  // (s_max_nb was zeroed before the barrier above)
     if (lane == 31) warp_tot[warp] = incl;
     __syncthreads();
     int run = incl - local;
@@ -156,7 +202,6 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   // exactly the consecutive warps owner_warp(first block) .. owner_warp(last).
   const int64_t W = min((int64_t)gridDim.x * WARPS, TB);
   const int gw = blockIdx.x * WARPS + warp;
-  if (gw >= W) return;
 
   // Sequences with no context produce zeros (CTA 0 writes them).
   if (blockIdx.x == 0) {
@@ -170,10 +215,20 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   }
   if (TB == 0) return;
 
-  const int64_t f0 = (int64_t)gw * TB / W;
-  const int64_t f1 = (int64_t)(gw + 1) * TB / W;
+  // Merge mode, the same in every CTA: when every split (sequence, kv head)
+  // has few contributor warps, the last one to finish merges it (no global
+  // wait); when a long sequence spreads over many warps, all warps meet at a
+  // grid barrier and the merges are spread over the contributors.
+  bool barrier_mode = false;
+  if (TB > 0) {
+    const int64_t per_warp = TB / W;  // >= 1
+    const int max_nb = s_max_nb;
+    barrier_mode = (max_nb + per_warp - 1) / per_warp + 1 > kMaxLastArriver;
+  }
+  // Warps past W own nothing but still take part in the grid barrier below.
+  const int64_t f0 = gw < W ? (int64_t)gw * TB / W : TB;
+  const int64_t f1 = gw < W ? (int64_t)(gw + 1) * TB / W : TB;
   const int nwork = (int)(f1 - f0);
-  if (nwork <= 0) return;
 
   // Locate flat index f0: sequence b (largest with Hkv*prefix[b] <= f0).
   auto locate = [&](int64_t f, int& b, int& kvh, int& j) {
@@ -191,6 +246,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     j = (int)(off - (int64_t)kvh * nb);
   };
 
+  if (nwork > 0) {
   const uint32_t ring = base_u32 + warp * STAGES * STAGE;
   uint64_t* wbars = bars + warp * STAGES;
   int* winfo = info + warp * STAGES;
@@ -487,9 +543,10 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         if (n0 < G) { pp->o[n0][d0] = o[t][0]; pp->o[n0][d0 + 8] = o[t][2]; }
         if (n1 < G) { pp->o[n1][d0] = o[t][1]; pp->o[n1][d0 + 8] = o[t][3]; }
       }
+      if (!barrier_mode) {
       __threadfence();
       __syncwarp();
-      const int cidx = cb * Hkv + ckvh;
+      const int cidx = 2 + cb * Hkv + ckvh;  // [0..1]: grid barrier words
       const int wa = owner_warp(seg_S, TB, W), wb = owner_warp(seg_E - 1, TB, W);
       const int ncontrib = wb - wa + 1;
       int old = 0;
@@ -584,6 +641,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         }
         if (lane == 0) a.counters[cidx] = 0;
       }
+      }  // !barrier_mode
     }
     // advance consumer to the next segment
     cj = 0;
@@ -598,6 +656,71 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     for (int k = i + 1; k < min(nwork, i + STAGES); k++) {
       const int slot = k % STAGES;
       if (!mbar_wait_warp(smem_u32(&wbars[slot]), (uint32_t)((k / STAGES) & 1), a.status)) break;
+    }
+  }
+  }  // nwork > 0
+
+  // ---- every partial triple is written: merge the split (sequence, kv head)
+  // pairs. Head n of a pair is merged by its contributor warp (n mod count),
+  // so the merges of long sequences spread over many warps.
+  if (!barrier_mode) return;
+  if (!grid_barrier(a.counters, a.status) || nwork <= 0) return;
+  auto slot_of = [&](int c, int wa, int64_t S) -> const Partial* {
+    const int64_t fc = (int64_t)c * TB / W;
+    return a.partials + 2 * c + ((c == wa && fc < S) ? 1 : 0);
+  };
+  for (int pass = 0; pass < 2; pass++) {
+    int b, kvh, j;
+    locate(pass == 0 ? f0 : f1 - 1, b, kvh, j);
+    const int nb = prefix[b + 1] - prefix[b];
+    const int64_t S = (int64_t)prefix[b] * Hkv + (int64_t)kvh * nb, E = S + nb;
+    if (pass == 1 && S <= f0) break;       // the last segment is the first one
+    if (S >= f0 && E <= f1) continue;      // whole: already written
+    const int wa = owner_warp(S, TB, W), wb = owner_warp(E - 1, TB, W);
+    const int nc = wb - wa + 1;
+    const int G = a.G;
+    for (int n = gw - wa; n < G; n += nc) {
+      float M = -INFINITY;
+      for (int c0 = 0; c0 < nc; c0 += 32)
+        if (c0 + lane < nc) M = fmaxf(M, __ldcg(&slot_of(wa + c0 + lane, wa, S)->m[n]));
+#pragma unroll
+      for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float den = 0.f;
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c0 = 0; c0 < nc; c0 += 32) {
+        float wl = 0.f;
+        if (c0 + lane < nc) {
+          const Partial* pc = slot_of(wa + c0 + lane, wa, S);
+          const float mc = __ldcg(&pc->m[n]);
+          wl = (mc == -INFINITY) ? 0.f : __expf(mc - M);
+          den += wl * __ldcg(&pc->l[n]);
+        }
+        const int cnt = min(32, nc - c0);
+        for (int k0 = 0; k0 < cnt; k0 += 8) {
+          float4 x[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++)  // eight rows in flight
+            x[u] = (k0 + u < cnt)
+                       ? __ldcg(reinterpret_cast<const float4*>(&slot_of(wa + c0 + k0 + u, wa, S)->o[n][0]) + lane)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const float w = __shfl_sync(0xffffffffu, wl, (k0 + u) & 31);
+            if (k0 + u < cnt) {
+              num.x += w * x[u].x; num.y += w * x[u].y; num.z += w * x[u].z; num.w += w * x[u].w;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(a.out + ((int64_t)b * a.H + kvh * G + n) * D)[lane] = pk;
     }
   }
 }
@@ -629,6 +752,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 #endif
 constexpr int kWarps = ZL_DECODE_WARPS;
 constexpr int kStages = ZL_DECODE_STAGES;
+
+// Cooperative launch: the grid (one CTA per SM) must be co-resident because its
+// CTAs meet at a grid barrier before merging split partials.
+template <typename Kern>
+cudaError_t launch_cooperative(Kern kern, int grid, int smem, cudaStream_t st, const DecodeArgs& args,
+                               const CUtensorMap& tk, const CUtensorMap& tv) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args, tk, tv);
+}
 
 }  // namespace
 
@@ -679,7 +820,7 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
   const int64_t W = (int64_t)grid * kWarps;
   s = ensure_workspace(ctx, sizeof(Partial) * 2 * W);
   if (s != ZL_OK) return s;
-  s = ensure_counters(ctx, sizeof(int) * (size_t)B * Hkv);
+  s = ensure_counters(ctx, sizeof(int) * (2 + (size_t)B * Hkv));
   if (s != ZL_OK) return s;
 
   DecodeArgs args;
@@ -701,7 +842,7 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
     ZL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal));
     attr_set = true;
   }
-  kern<<<grid, kWarps * 32, SM::kTotal, st>>>(args, tk, tv);
+  ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
   ZL_LAUNCH_CHECK(ctx);
   return ZL_OK;
 }
@@ -735,7 +876,7 @@ constexpr int kNoAllocMaxSegments = 16384;      // (sequence, kv head) pairs per
 struct NoAllocScratch {
   Partial partials[2 * kNoAllocMaxCtas * kWarps];
   int status;                          // device flags when the caller passes no status word
-  int counters[kNoAllocMaxSegments];   // must directly follow `status` (cleared together)
+  int counters[2 + kNoAllocMaxSegments];  // must directly follow `status` (cleared together)
 };
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
@@ -822,10 +963,10 @@ extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, 
 
   cudaStream_t st = S(stream);
   NoAllocScratch* scr = nd->scratch;
-  // The merge counters (and the fallback status word in front of them) must
-  // start at zero; clearing them per call also recovers from a call whose
-  // kernel gave up part-way.
-  e = cudaMemsetAsync(&scr->status, 0, sizeof(int) * (1 + (size_t)num_seqs * num_kv_heads), st);
+  // The merge counters and grid-barrier words (and the fallback status word in
+  // front of them) must start at zero; clearing them per call also recovers
+  // from a call whose kernel gave up part-way.
+  e = cudaMemsetAsync(&scr->status, 0, sizeof(int) * (3 + (size_t)num_seqs * num_kv_heads), st);
   if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: counter clear: %s", cudaGetErrorString(e));
 
   DecodeArgs args;
@@ -843,8 +984,8 @@ extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, 
   args.scale_log2 = resolve_scale(scale, D) * LOG2E;
   const int grid = nd->num_sms < kNoAllocMaxCtas ? nd->num_sms : kNoAllocMaxCtas;
   using SM = Smem<kWarps, kStages>;
-  paged_decode_bf16_kernel<kWarps, kStages><<<grid, kWarps * 32, SM::kTotal, st>>>(args, tk, tv);
-  e = cudaGetLastError();
+  e = launch_cooperative(paged_decode_bf16_kernel<kWarps, kStages>, grid, SM::kTotal, st, args, tk, tv);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: launch: %s", cudaGetErrorString(e));
   return ZL_OK;
 }
