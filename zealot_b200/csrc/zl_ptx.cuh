@@ -28,16 +28,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// Non-blocking probe of a phase (mbarrier.test_wait never suspends the
-// thread, so the polling loop below always regains control).
+// Probe of a phase that may suspend the thread until the phase completes,
+// for at most kSuspendNs (the explicit suspend-time hint bounds every call,
+// so the polling loops below always regain control). Waking on completion
+// instead of sleeping a fixed time keeps producer -> consumer hand-offs short.
+constexpr uint32_t kSuspendNs = 20000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -53,8 +56,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* st
   const long long t0 = clock64();
   for (uint32_t it = 1;; it++) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (it > 64) __nanosleep(32);
-    if ((it & 255) == 0 && aborted(status)) return false;
+    if ((it & 15) == 0 && aborted(status)) return false;
     if (clock64() - t0 > kWaitCycles) {
       atomicOr(status, 2 /* ZL_DEV_TIMEOUT */);
       return false;
@@ -69,8 +71,7 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, in
   const long long t0 = clock64();
   for (uint32_t it = 0;; it++) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-    if (it > 64) __nanosleep(32);
-    const bool ab = (it & 255) == 255 && aborted(status);
+    const bool ab = (it & 15) == 15 && aborted(status);
     const bool to = clock64() - t0 > kWaitCycles;
     if (__any_sync(0xffffffffu, ab || to)) {
       if (to && (threadIdx.x & 31) == 0) atomicOr(status, 2 /* ZL_DEV_TIMEOUT */);
