@@ -837,10 +837,11 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
 
   using SM = Smem<kWarps, kStages>;
   auto kern = paged_decode_bf16_kernel<kWarps, kStages>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the shared-memory limit is a per-device attribute of the function
+  static std::atomic<uint64_t> attr_set{0};
+  if (ctx->device < 64 && !(attr_set.load() & (1ull << ctx->device))) {
     ZL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal));
-    attr_set = true;
+    attr_set.fetch_or(1ull << ctx->device);
   }
   ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
   ZL_LAUNCH_CHECK(ctx);

@@ -356,11 +356,12 @@ zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const voi
   args.H = H; args.Hkv = Hkv; args.G = H / Hkv; args.num_seqs = num_seqs;
   args.scale_log2 = scale * LOG2E;
   args.causal = causal ? 1 : 0;
-  static bool attr = false;
-  if (!attr) {
+  // the shared-memory limit is a per-device attribute of the function
+  static std::atomic<uint64_t> attr_set{0};
+  if (ctx->device < 64 && !(attr_set.load() & (1ull << ctx->device))) {
     ZL_CUDA_TRY(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Smem::kTotal));
-    attr = true;
+    attr_set.fetch_or(1ull << ctx->device);
   }
   dim3 grid((unsigned)(num_seqs * (H / NQ)), (unsigned)max_tiles);
   prefill_tc_kernel<<<grid, THREADS, Smem::kTotal, st>>>(args, tq, tk, tv);
