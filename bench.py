@@ -436,6 +436,140 @@ def run_side_only(args):
     ctx.close()
 
 
+C4 = dict(prefill_chunks=8, chunk_len=512, decode_seqs=248, ctx=(1024, 8192), seed=404)
+
+
+def run_c4(args):
+    """--workload c4: one engine step of a Mistral-7B-shaped decoder (32 layers,
+    d_model 4096, 32/8 heads, d 128, intermediate 14336, vocab 32000, random bf16
+    weights): 8 prefill chunks x 512 tokens + 248 decode sequences with context
+    U{1024..8192}, batched into one zl_decoder_step. tokens/s = rows per step / step
+    time. Inputs (14.5 GB of weights, ~147 GB of KV) are far larger than L2."""
+    import torch
+    import zealot_b200 as zb
+    from zealot_b200.decoder import Decoder, DecoderConfig, StepBatch, random_weights
+    torch.cuda.set_device(0)
+    cfg = DecoderConfig.mistral_7b()
+    rng = np.random.default_rng(C4["seed"])
+    dlens = rng.integers(C4["ctx"][0], C4["ctx"][1] + 1, size=C4["decode_seqs"]).astype(np.int32)
+    P = C4["prefill_chunks"] * C4["chunk_len"]
+    nblk_dec = (dlens + BS - 1) // BS
+    nblk = int(nblk_dec.sum()) + C4["prefill_chunks"] * (C4["chunk_len"] // BS)
+    pool_bytes = nblk * cfg.num_kv_heads * BS * cfg.head_dim * 2
+    weight_bytes = 2 * (cfg.num_layers * sum(int(np.prod(s)) for s in cfg.layer_shapes().values())
+                        + 2 * cfg.vocab * cfg.hidden + cfg.hidden)
+    need = 2 * cfg.num_layers * pool_bytes + weight_bytes + (4 << 30)
+    free, _ = torch.cuda.mem_get_info(0)
+    if free < need:
+        raise SystemExit(f"c4 needs {need / 1e9:.1f} GB of device memory, {free / 1e9:.1f} GB free")
+    perm = rng.permutation(nblk).astype(np.int32)
+    mb = int(nblk_dec.max())
+    dtab = np.full((len(dlens), mb), -1, np.int32)
+    off = 0
+    for i, n in enumerate(nblk_dec):
+        dtab[i, :n] = perm[off: off + n]
+        off += n
+    ptabs = []
+    for c in range(C4["prefill_chunks"]):
+        n = C4["chunk_len"] // BS
+        ptabs.append(list(perm[off: off + n]))
+        off += n
+    chunks = [rng.integers(0, cfg.vocab, C4["chunk_len"]) for _ in range(C4["prefill_chunks"])]
+    dtoks = rng.integers(0, cfg.vocab, len(dlens))
+    batch = StepBatch.build(chunks, dtoks, dtab, dlens, ptabs, BS)
+    T = P + len(dlens)
+    log(f"c4: building weights ({weight_bytes / 1e9:.1f} GB) and pools "
+        f"({2 * cfg.num_layers * pool_bytes / 1e9:.1f} GB)")
+    w = random_weights(cfg, seed=C4["seed"])
+    g = torch.Generator(device="cuda").manual_seed(C4["seed"])
+    shape = (nblk, cfg.num_kv_heads, BS, cfg.head_dim)
+    kps = [torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16)
+           for _ in range(cfg.num_layers)]
+    vps = [torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16)
+           for _ in range(cfg.num_layers)]
+    ctx = zb.GpuContext(0)
+    dec = Decoder(ctx, cfg, w)
+    stream = torch.cuda.Stream(0)
+    sh = stream.cuda_stream
+    logits = torch.empty((batch.num_last, cfg.vocab), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        dec.step(batch, kps, vps, BS, logits=logits, stream=sh)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.check_status(sh)
+    clocks = ClockSampler(0)
+    clocks.start()
+    launches0 = ctx.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = ctx.launch_count() - launches0
+    ctx.check_status(sh)
+
+    # parts of the step timed alone: the attention kernels over all layers
+    attn = zb.CudaAttention(ctx)
+    Hq, Hk, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+    q = torch.randn((T, Hq, d), device="cuda", dtype=torch.bfloat16)
+    kv = torch.randn((P, Hk, d), device="cuda", dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+
+    def time_it(fn, n=3):
+        for _ in range(2):
+            fn()
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def dec_all():
+        for l in range(cfg.num_layers):
+            attn.paged_forward(q[P:], kps[l], vps[l], batch.block_tables, batch.seq_lens, o[P:],
+                               len(dlens), Hq, Hk, d, BS, mb, stream=sh)
+
+    def pre_all():
+        for l in range(cfg.num_layers):
+            attn.forward_gpu(q[:P], kv, kv, batch.cu_prefill, o[:P], Hq, Hk, d, C4["chunk_len"],
+                             causal=True, stream=sh)
+
+    ms_dec, ms_pre = time_it(dec_all), time_it(pre_all)
+    ctx.check_status(sh)
+    peaks = load_peaks()
+    params_layer = sum(int(np.prod(s)) for k, s in cfg.layer_shapes().items() if len(s) == 2)
+    gemm_flop = 2.0 * T * params_layer * cfg.num_layers + 2.0 * batch.num_last * cfg.vocab * cfg.hidden
+    pre_flop = cfg.num_layers * C4["prefill_chunks"] * 4 * Hq * d * C4["chunk_len"] * (C4["chunk_len"] + 1) / 2
+    kv_bytes = cfg.num_layers * float(dlens.astype(np.int64).sum()) * Hk * d * 2 * 2
+    ideal_ms = 1e3 * ((gemm_flop + pre_flop) / (peaks["bf16_tflops"] * 1e12) + kv_bytes / (peaks["hbm_gbs"] * 1e9))
+    line = {"metric": "engine_step_tokens_per_s", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random bf16 weights and KV)",
+            "config": {"workload": "C4 engine step, Mistral-7B shape (32 layers, d_model 4096, 32/8 heads, "
+                                   "d 128, intermediate 14336, vocab 32000): 8 prefill chunks x 512 + "
+                                   "248 decode seqs, ctx U[1024,8192]; inputs larger than L2",
+                       "rows_per_step": T, "kv_tokens": int(dlens.sum())},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor+hbm", "ideal_ms": round(ideal_ms, 3), "frac": round(ideal_ms / ms, 4),
+                         "gemm_tflop": round(gemm_flop / 1e12, 3), "prefill_attn_tflop": round(pre_flop / 1e12, 3),
+                         "decode_kv_gb": round(kv_bytes / 1e9, 2), "peaks": peaks},
+            "parts_ms": {"paged_decode_32_layers": round(ms_dec, 3), "prefill_32_layers": round(ms_pre, 3),
+                         "rest (GEMMs, norms, cache writes)": round(ms - ms_dec - ms_pre, 3),
+                         "gemm_tflops_if_rest": round(gemm_flop / ((ms - ms_dec - ms_pre) * 1e-3) / 1e12, 1)},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -536,9 +670,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-side", action="store_true", help="skip the prefill / cache side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "c5", "prefill", "cache"], default="decode",
-                    help="decode (C2, the headline), c5 (long-context decode), or a single side kernel "
-                         "on its C3 workload")
+    ap.add_argument("--workload", choices=["decode", "c5", "prefill", "cache", "c4"], default="decode",
+                    help="decode (C2, the headline), c5 (long-context decode), a single side kernel "
+                         "on its C3 workload, or c4 (a full Mistral-7B-shaped engine step, 1 GPU)")
     ap.add_argument("--lite", action="store_true",
                     help="only warm-up + timed steps of the kernel (no clock soak, e2e, side runs or "
                          "CPU baseline): the form used under ncu")
@@ -559,6 +693,11 @@ def main():
         return
     if args.workload in ("prefill", "cache"):
         run_side_only(args)
+        return
+    if args.workload == "c4":
+        if world > 1:
+            raise SystemExit("--workload c4 runs on one GPU")
+        run_c4(args)
         return
     if args.workload == "c5":
         args.no_side = True

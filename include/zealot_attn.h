@@ -280,6 +280,61 @@ zl_status zl_runner_step(zl_runner* r, const zl_seq_input* batch, int n, float* 
 /* ModelRunner::drop_state (src/engine.rs:22). Unknown ids are ignored. */
 zl_status zl_runner_drop_state(zl_runner* r, const char* request_id);
 
+/* ---------------------------------------------------------------------------
+ * Engine step of a full decoder (the layer loop of src/cuda_runner.rs:303-607:
+ * RMSNorm -> q/k/v -> paged KV -> attention -> o-proj + residual -> RMSNorm ->
+ * gate/up -> silu(gate)*up -> down + residual; final RMSNorm -> lm_head on the
+ * last row of each sequence), batched over every sequence of the step: one
+ * GEMM per projection per layer, not one per sequence. bf16 weights and
+ * activations, fp32 accumulation; RMSNorm eps as given (the reference passes
+ * 1e-6). All pointers are device pointers owned by the caller.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  const void* attn_norm;  /* [hidden] bf16                                    */
+  const void* wq;         /* [H*d][hidden] bf16, torch Linear layout (out,in) */
+  const void* wk;         /* [Hkv*d][hidden]                                  */
+  const void* wv;         /* [Hkv*d][hidden]                                  */
+  const void* wo;         /* [hidden][H*d]                                    */
+  const void* mlp_norm;   /* [hidden]                                         */
+  const void* w_gate_up;  /* [2*inter][hidden]: gate rows, then up rows       */
+  const void* w_down;     /* [hidden][inter]                                  */
+} zl_layer_weights;
+
+typedef struct {
+  int num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate;
+  int64_t vocab;
+  float rms_eps;
+  const void* embed;              /* [vocab][hidden] bf16 */
+  const zl_layer_weights* layers; /* host array [num_layers] of device pointers */
+  const void* final_norm;         /* [hidden] */
+  const void* lm_head;            /* [vocab][hidden] */
+} zl_decoder;
+
+/* Rows [0, prefill_tokens) are prefill chunks packed back to back (sequence i
+ * is rows cu_prefill[i]..cu_prefill[i+1]; each chunk attends causally to
+ * itself); rows [prefill_tokens, prefill_tokens + num_decode) are one decode
+ * token per sequence, attending through its block table over seq_lens[i]
+ * cached tokens (its own K/V included, written by this step). */
+typedef struct {
+  const int64_t* tokens;       /* [T] token ids, T = prefill_tokens + num_decode */
+  const int64_t* slot_mapping; /* [T] pool slot of each row's K/V               */
+  const int32_t* cu_prefill;   /* [num_prefill+1]                               */
+  int num_prefill, max_prefill_len;
+  int64_t prefill_tokens;
+  const int32_t* block_tables; /* [num_decode][max_blocks_per_seq], -1 padded   */
+  const int32_t* seq_lens;     /* [num_decode]                                  */
+  int num_decode, max_blocks_per_seq;
+  const int32_t* last_rows;    /* [num_last] rows whose logits are produced     */
+  int num_last;
+} zl_step_batch;
+
+/* logits: device fp32 [num_last][vocab]. k_pools / v_pools: host arrays of
+ * num_layers device pools, [num_blocks][Hkv][block_size][d] bf16 each.
+ * Prefill chunks start at position 0 of their sequence (no cached prefix). */
+zl_status zl_decoder_step(zl_ctx* ctx, const zl_decoder* model, void* const* k_pools,
+                          void* const* v_pools, int64_t num_blocks, int block_size,
+                          const zl_step_batch* batch, float* logits, zl_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

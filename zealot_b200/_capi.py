@@ -43,6 +43,25 @@ class zl_seq_input(ctypes.Structure):
                 ("is_prefill", c_int), ("prefill_pos", c_int)]
 
 
+class zl_layer_weights(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("attn_norm", "wq", "wk", "wv", "wo", "mlp_norm",
+                                        "w_gate_up", "w_down")]
+
+
+class zl_decoder(ctypes.Structure):
+    _fields_ = [("num_layers", c_int), ("hidden", c_int), ("num_heads", c_int),
+                ("num_kv_heads", c_int), ("head_dim", c_int), ("intermediate", c_int),
+                ("vocab", c_int64), ("rms_eps", c_float), ("embed", c_void_p),
+                ("layers", P(zl_layer_weights)), ("final_norm", c_void_p), ("lm_head", c_void_p)]
+
+
+class zl_step_batch(ctypes.Structure):
+    _fields_ = [("tokens", c_void_p), ("slot_mapping", c_void_p), ("cu_prefill", c_void_p),
+                ("num_prefill", c_int), ("max_prefill_len", c_int), ("prefill_tokens", c_int64),
+                ("block_tables", c_void_p), ("seq_lens", c_void_p), ("num_decode", c_int),
+                ("max_blocks_per_seq", c_int), ("last_rows", c_void_p), ("num_last", c_int)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/zealot_attn.h
 SIGNATURES = {
     "zl_ctx_create": (c_int, [P(zl_ctx_cfg), P(c_void_p)]),
@@ -97,6 +116,8 @@ SIGNATURES = {
     "zl_runner_destroy": (c_int, [c_void_p]),
     "zl_runner_step": (c_int, [c_void_p, P(zl_seq_input), c_int, P(c_float)]),
     "zl_runner_drop_state": (c_int, [c_void_p, c_char_p]),
+    "zl_decoder_step": (c_int, [c_void_p, P(zl_decoder), P(c_void_p), P(c_void_p), c_int64, c_int,
+                                P(zl_step_batch), c_void_p, c_void_p]),
 }
 
 _lib = None
@@ -108,7 +129,7 @@ def load(path: str = LIB_PATH):
     global _lib
     if _lib is None:
         if not os.path.exists(path):
-            raise ImportError(f"{path} is missing: build it with `python -m zealot_b200.build`")
+            raise ImportError(f"{path} is missing: build it with `python zealot_b200/build.py`")
         lib = ctypes.CDLL(path)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(lib, name)

@@ -1,7 +1,10 @@
 """Builds libzealot_attn.so in-tree with nvcc for sm_100a.
 
-    python -m zealot_b200.build            # incremental
-    python -m zealot_b200.build --force    # rebuild everything
+    python zealot_b200/build.py            # incremental
+    python zealot_b200/build.py --force    # rebuild everything
+
+(run as a file, not with -m: importing the package loads the library, which
+does not exist yet on a fresh checkout)
 
 Every .cu / .cc file under zealot_b200/csrc is compiled with
 -gencode arch=compute_100a,code=sm_100a and linked into

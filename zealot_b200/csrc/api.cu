@@ -136,6 +136,7 @@ zl_status zl_ctx_destroy(zl_ctx* ctx) {
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->gather_buf) cudaFree(ctx->gather_buf);
+  if (ctx->activations) cudaFree(ctx->activations);
   delete ctx;
   return ZL_OK;
 }

@@ -32,6 +32,9 @@ struct zl_ctx {
   int nranks = 1, rank = 0;
   void* gather_buf = nullptr;
   size_t gather_bytes = 0;
+  // decoder-step activations (residual stream, q/k/v, attention out, MLP)
+  void* activations = nullptr;
+  size_t activation_bytes = 0;
 };
 
 namespace zl {
