@@ -544,6 +544,41 @@ def run_c4(args):
 
     ms_dec, ms_pre = time_it(dec_all), time_it(pre_all)
     ctx.check_status(sh)
+
+    # sampling the step's rows on the device vs copying the logits to the host
+    from zealot_b200.sampling import GpuSampler, SamplingParams
+    sampler = GpuSampler(ctx)
+    kinds = [SamplingParams(temperature=0.0), SamplingParams(temperature=0.7, top_k=50, top_p=0.9),
+             SamplingParams(top_p=0.95, repetition_penalty=1.1)]
+    sparams = [kinds[i % 3] for i in range(batch.num_last)]
+    prev = [list(rng.integers(0, cfg.vocab, 64)) for _ in range(batch.num_last)]
+    unif = torch.from_numpy(rng.random(batch.num_last).astype(np.float32)).cuda()
+    t0 = time.perf_counter()
+    sbatch = sampler.prepare(batch.num_last, cfg.vocab, sparams, prev)
+    torch.cuda.synchronize()
+    ms_prep = (time.perf_counter() - t0) * 1e3
+    sout = sampler.launch(sbatch, logits, unif, stream=sh)
+    ms_sample = time_it(lambda: sampler.launch(sbatch, logits, unif, out=sout, stream=sh), n=10)
+    # the same rows on the host: the restated reference sampler, a bounded sample of rows
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as _oracle
+    host_logits_np = logits.cpu().numpy()
+    ur = unif.cpu().numpy()
+    n_cpu = 24
+    t0 = time.perf_counter()
+    for i in range(n_cpu):
+        p = sparams[i]
+        _oracle.sample(host_logits_np[i], prev=prev[i], temperature=p.temperature, top_k=p.top_k,
+                       top_p=p.top_p, repetition_penalty=p.repetition_penalty, r=float(ur[i]))
+    ms_cpu_row = (time.perf_counter() - t0) * 1e3 / n_cpu
+    host_logits = torch.empty(logits.shape, dtype=torch.float32, pin_memory=True)
+
+    def d2h():
+        with torch.cuda.stream(stream):
+            host_logits.copy_(logits, non_blocking=True)
+
+    ms_d2h = time_it(d2h, n=10)
+    ctx.check_status(sh)
     peaks = load_peaks()
     params_layer = sum(int(np.prod(s)) for k, s in cfg.layer_shapes().items() if len(s) == 2)
     gemm_flop = 2.0 * T * params_layer * cfg.num_layers + 2.0 * batch.num_last * cfg.vocab * cfg.hidden
@@ -565,6 +600,16 @@ def run_c4(args):
             "parts_ms": {"paged_decode_32_layers": round(ms_dec, 3), "prefill_32_layers": round(ms_pre, 3),
                          "rest (GEMMs, norms, cache writes)": round(ms - ms_dec - ms_pre, 3),
                          "gemm_tflops_if_rest": round(gemm_flop / ((ms - ms_dec - ms_pre) * 1e-3) / 1e12, 1)},
+            "sampling": {"rows": batch.num_last, "vocab": cfg.vocab,
+                         "params": "greedy / t0.7 top-k 50 top-p 0.9 / top-p 0.95 + repetition 1.1, 64 previous ids",
+                         "zl_sample_kernel_ms": round(ms_sample, 4),
+                         "host_prepare_ms": round(ms_prep, 3),
+                         "logits_d2h_ms": round(ms_d2h, 4),
+                         "cpu_reference_ms": round(ms_cpu_row * batch.num_last, 2),
+                         "note": "kernel = one zl_sample launch over device-resident inputs (CUDA events); "
+                                 "host_prepare = packing params / penalty lists and their H2D (wall clock, once "
+                                 "per step); cpu_reference = the restated reference sampler (oracle, 1 thread) "
+                                 f"timed on {n_cpu} rows and scaled to all rows, plus the logits D2H it needs"},
             "clocks": clk}
     print(json.dumps(line), flush=True)
     ctx.close()

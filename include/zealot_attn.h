@@ -328,6 +328,41 @@ typedef struct {
   int num_last;
 } zl_step_batch;
 
+/* ---------------------------------------------------------------------------
+ * Sampling on the GPU for every row of a step: Sampler::sample_with_mask
+ * (src/sampling.rs:77-230) per row, plus the engine's fallback to unconstrained
+ * sampling when the allowed-token mask leaves nothing (src/engine.rs:190-206)
+ * and token 0 when sampling still fails (src/engine.rs:214-217).
+ * ------------------------------------------------------------------------- */
+typedef struct {        /* SamplingParams (src/sampling.rs:22-45); seed stays with the caller */
+  float temperature;    /* 1.0 default; < 1e-7 = greedy */
+  int top_k;            /* 0 = off */
+  float top_p;          /* 0 = off; only 0 < top_p < 1 filters */
+  float repetition_penalty, frequency_penalty, presence_penalty;
+} zl_sampling_params;
+
+enum {
+  ZL_SAMPLE_ALL_MASKED = 1, /* SamplingError::AllTokensMasked: token 0, logprob -inf */
+  ZL_SAMPLE_FELL_BACK = 2   /* the mask left no token; sampled without it */
+};
+
+/* All pointers are device pointers. logits [num_rows][vocab] f32; params
+ * [num_rows]; allowed_bits [num_rows][ceil(mask_len/32)] (bit i = token i is
+ * allowed; tokens >= mask_len are allowed, as sampling.rs:91-93) or NULL;
+ * mask_rows [num_rows] (1 = the row is masked) or NULL for every row;
+ * penalty_offsets [num_rows+1] into penalty_ids / penalty_counts: the distinct
+ * previous output tokens of each row with their occurrence counts (NULL = no
+ * history); uniforms [num_rows]: the caller's draw r in [0, 1) per row (the
+ * reference's rng.gen_range(0.0..1.0), sampling.rs:277); fallback_unmasked:
+ * apply the engine's fallback. Outputs token_ids, logprobs, row_status
+ * (ZL_SAMPLE_* bits; may be NULL). vocab == 0 is EmptyLogits: ZL_ERR_INVALID_ARG. */
+zl_status zl_sample(zl_ctx* ctx, const float* logits, int num_rows, int64_t vocab,
+                    const zl_sampling_params* params, const uint32_t* allowed_bits,
+                    const uint8_t* mask_rows, int64_t mask_len, const int32_t* penalty_offsets,
+                    const int64_t* penalty_ids, const int32_t* penalty_counts, const float* uniforms,
+                    int fallback_unmasked, int64_t* token_ids, float* logprobs, int32_t* row_status,
+                    zl_stream stream);
+
 /* logits: device fp32 [num_last][vocab]. k_pools / v_pools: host arrays of
  * num_layers device pools, [num_blocks][Hkv][block_size][d] bf16 each.
  * Prefill chunks start at position 0 of their sequence (no cached prefix). */

@@ -67,6 +67,10 @@ def lib():
         L.zlo_argmax.restype = ctypes.c_int64
         L.zlo_f32_to_bf16.argtypes = [_f32p, _u16p, _sz]
         L.zlo_bf16_to_f32.argtypes = [_u16p, _f32p, _sz]
+        _f = ctypes.c_float
+        L.zlo_sample.argtypes = [_f32p, _sz, _i64p, _sz, _f, ctypes.c_uint32, _f, _f, _f, _f, _u8p, _sz,
+                                 _f, ctypes.c_int, _i64p, _f32p, ctypes.POINTER(ctypes.c_double)]
+        L.zlo_sample.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -253,6 +257,46 @@ def argmax(x) -> int:
     """src/sampling.rs:233-243: first maximum wins."""
     x = _f32(x).reshape(-1)
     return int(lib().zlo_argmax(_p(x, _f32p), x.size))
+
+
+EMPTY_LOGITS, ALL_TOKENS_MASKED = 1, 2  # SamplingError (src/sampling.rs:15-20)
+
+
+def sample(logits, prev=(), temperature=1.0, top_k=0, top_p=0.0, repetition_penalty=1.0,
+           frequency_penalty=0.0, presence_penalty=0.0, mask=None, r=0.5, exact=False):
+    """src/sampling.rs:77-230 (Sampler::sample_with_mask) with `r` the rng draw.
+    Returns (status, token, logprob, margin): status 0, EMPTY_LOGITS or
+    ALL_TOKENS_MASKED; margin = the closest a float decision came to flipping.
+    exact=True: the same decisions with every sum in double (see zl_oracle.h)."""
+    x = _f32(logits).reshape(-1)
+    pv = np.ascontiguousarray(prev, dtype=np.int64).reshape(-1)
+    if pv.size == 0:
+        pv = np.zeros(1, np.int64)
+        n_prev = 0
+    else:
+        n_prev = pv.size
+    if x.size == 0:
+        x = np.zeros(1, np.float32)
+        n = 0
+    else:
+        n = x.size
+    if mask is None:
+        mp, mlen = ctypes.POINTER(ctypes.c_uint8)(), 0
+    else:
+        m = np.ascontiguousarray(mask, dtype=np.uint8).reshape(-1)
+        if m.size == 0:
+            m = np.zeros(1, np.uint8)
+            mlen = 0
+        else:
+            mlen = m.size
+        mp = _p(m, _u8p)
+    tok = np.zeros(1, np.int64)
+    lp = np.zeros(1, np.float32)
+    margin = ctypes.c_double()
+    rc = lib().zlo_sample(_p(x, _f32p), n, _p(pv, _i64p), n_prev, temperature, top_k, top_p,
+                          repetition_penalty, frequency_penalty, presence_penalty, mp, mlen, r,
+                          int(exact), _p(tok, _i64p), _p(lp, _f32p), ctypes.byref(margin))
+    return rc, int(tok[0]), float(lp[0]), float(margin.value)
 
 
 def f32_to_bf16_bits(x) -> np.ndarray:

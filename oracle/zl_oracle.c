@@ -410,6 +410,182 @@ int64_t zlo_argmax(const float* x, size_t n) {
   return best_idx;
 }
 
+/* ---- sampling (src/sampling.rs) ---- */
+
+typedef struct {
+  float v; /* probability */
+  float s; /* score */
+  size_t i;
+} zlo_vi;
+
+/* partial_cmp(..).unwrap_or(Equal), descending (sampling.rs:170-172) */
+static int cmp_desc_value(const void* a, const void* b) {
+  const float x = *(const float*)a, y = *(const float*)b;
+  return (y > x) - (y < x);
+}
+/* descending probability; equal probabilities (left to sort_unstable by the
+ * reference) by descending score, then ascending index */
+static int cmp_desc_vi(const void* a, const void* b) {
+  const zlo_vi* x = (const zlo_vi*)a;
+  const zlo_vi* y = (const zlo_vi*)b;
+  if (y->v > x->v) return 1;
+  if (y->v < x->v) return -1;
+  if (y->s > x->s) return 1;
+  if (y->s < x->s) return -1;
+  return (x->i > y->i) - (x->i < y->i);
+}
+static int cmp_i64(const void* a, const void* b) {
+  const int64_t x = *(const int64_t*)a, y = *(const int64_t*)b;
+  return (x > y) - (x < y);
+}
+
+/* softmax (sampling.rs:254-273). exact: the sum in double, rounded to f32 once. */
+static void zlo_softmax(const float* s, float* p, size_t n, int exact) {
+  float max = -INFINITY;
+  for (size_t i = 0; i < n; i++)
+    if (isfinite(s[i])) max = fmaxf(max, s[i]);
+  float sum = 0.f;
+  double dsum = 0.0;
+  for (size_t i = 0; i < n; i++) {
+    p[i] = isfinite(s[i]) ? expf(s[i] - max) : 0.f;
+    sum += p[i];
+    dsum += p[i];
+  }
+  if (exact) sum = (float)dsum;
+  if (sum > 0.f)
+    for (size_t i = 0; i < n; i++) p[i] /= sum;
+}
+
+int zlo_sample(const float* logits, size_t n, const int64_t* prev, size_t n_prev, float temperature,
+               uint32_t top_k, float top_p, float repetition_penalty, float frequency_penalty,
+               float presence_penalty, const uint8_t* mask, size_t mask_len, float r, int exact,
+               int64_t* token, float* logprob, double* margin) {
+  *margin = INFINITY;
+  if (n == 0) return 1;
+  float* s = (float*)malloc(n * sizeof(float));
+  float* probs = (float*)malloc(n * sizeof(float));
+  memcpy(s, logits, n * sizeof(float));
+  int rc = 0;
+  /* 0. constraint mask (:88-100) */
+  if (mask) {
+    int any = 0;
+    for (size_t i = 0; i < n; i++) {
+      if (i < mask_len && !mask[i]) s[i] = -INFINITY;
+      any |= isfinite(s[i]);
+    }
+    if (!any) { rc = 2; goto out; }
+  }
+  /* 1. greedy (:103-110) with lightweight_logprob (:246-251) */
+  if (temperature < 1e-7f) {
+    const int64_t idx = zlo_argmax(s, n);
+    float max = -INFINITY;
+    for (size_t i = 0; i < n; i++) max = fmaxf(max, s[i]);
+    float sum = 0.f;
+    double dsum = 0.0;
+    for (size_t i = 0; i < n; i++) {
+      sum += expf(s[i] - max);
+      dsum += expf(s[i] - max);
+    }
+    if (exact) sum = (float)dsum;
+    *token = idx;
+    *logprob = logf(expf(s[idx] - max) / sum);
+    goto out;
+  }
+  /* 2. temperature (:114-119) */
+  if (temperature != 1.0f) {
+    const float inv_t = 1.0f / temperature;
+    for (size_t i = 0; i < n; i++) s[i] *= inv_t;
+  }
+  /* 3/4. presence + frequency penalties from the frequency map (:125-145) */
+  if ((presence_penalty != 0.f || frequency_penalty != 0.f) && n_prev > 0) {
+    int64_t* ids = (int64_t*)malloc(n_prev * sizeof(int64_t));
+    memcpy(ids, prev, n_prev * sizeof(int64_t));
+    qsort(ids, n_prev, sizeof(int64_t), cmp_i64);
+    for (size_t a = 0; a < n_prev;) {
+      size_t b = a;
+      while (b < n_prev && ids[b] == ids[a]) b++;
+      const int64_t id = ids[a];
+      const uint32_t count = (uint32_t)(b - a);
+      if (id >= 0 && (uint64_t)id < n) {
+        s[id] -= (float)count * frequency_penalty;
+        if (presence_penalty != 0.f) s[id] -= presence_penalty;
+      }
+      a = b;
+    }
+    free(ids);
+  }
+  /* 5. repetition penalty, per occurrence (:148-160) */
+  if (repetition_penalty != 1.0f && n_prev > 0) {
+    for (size_t j = 0; j < n_prev; j++) {
+      const int64_t id = prev[j];
+      if (id < 0 || (uint64_t)id >= n) continue;
+      if (s[id] > 0.f) s[id] /= repetition_penalty;
+      else s[id] *= repetition_penalty;
+    }
+  }
+  /* 6. top-k (:163-180) */
+  if (top_k > 0) {
+    const size_t k = top_k < n ? top_k : n;
+    if (k < n) {
+      float* sorted = (float*)malloc(n * sizeof(float));
+      memcpy(sorted, s, n * sizeof(float));
+      qsort(sorted, n, sizeof(float), cmp_desc_value);
+      const float thr = sorted[k - 1];
+      free(sorted);
+      for (size_t i = 0; i < n; i++)
+        if (s[i] < thr) s[i] = -INFINITY;
+    }
+  }
+  /* 7. top-p (:183-210) */
+  if (top_p > 0.f && top_p < 1.0f) {
+    zlo_softmax(s, probs, n, exact);
+    zlo_vi* idx = (zlo_vi*)malloc(n * sizeof(zlo_vi));
+    for (size_t i = 0; i < n; i++) { idx[i].v = probs[i]; idx[i].s = s[i]; idx[i].i = i; }
+    qsort(idx, n, sizeof(zlo_vi), cmp_desc_vi);
+    double cum = 0.0; /* f32 accumulation unless exact */
+    size_t selected = 0;
+    for (size_t j = 0; j < n; j++) {
+      const double before = cum;
+      cum = exact ? cum + (double)idx[j].v : (double)((float)cum + idx[j].v);
+      selected++;
+      if (cum >= (double)top_p) {
+        double m1 = fabs((double)cum - (double)top_p), m2 = fabs((double)top_p - (double)before);
+        *margin = fmin(*margin, fmin(m1, m2));
+        break;
+      }
+    }
+    for (size_t j = selected; j < n; j++) s[idx[j].i] = -INFINITY;
+    free(idx);
+  }
+  /* 8-9. softmax, all-masked check (:213-219) */
+  zlo_softmax(s, probs, n, exact);
+  {
+    float sum = 0.f;
+    for (size_t i = 0; i < n; i++) sum += probs[i];
+    if (sum == 0.f || !isfinite(sum)) { rc = 2; goto out; }
+  }
+  /* 10. multinomial (:275-290) */
+  {
+    double cumsum = 0.0; /* f32 accumulation unless exact */
+    size_t pick = n - 1;
+    for (size_t i = 0; i < n; i++) {
+      const double before = cumsum;
+      cumsum = exact ? cumsum + (double)probs[i] : (double)((float)cumsum + probs[i]);
+      if ((double)r < cumsum) {
+        pick = i;
+        *margin = fmin(*margin, fmin(fabs((double)cumsum - r), fabs((double)r - before)));
+        break;
+      }
+    }
+    *token = (int64_t)pick;
+    *logprob = logf(probs[pick]);
+  }
+out:
+  free(s);
+  free(probs);
+  return rc;
+}
+
 void zlo_f32_to_bf16(const float* src, uint16_t* dst, size_t n) {
   for (size_t i = 0; i < n; i++) {
     uint32_t u;

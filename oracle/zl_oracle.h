@@ -124,6 +124,23 @@ int zlo_prefill_varlen_rows(const float* q, const float* k, const float* v,
 /* src/sampling.rs:233-243 -- argmax, first maximum wins. */
 int64_t zlo_argmax(const float* x, size_t n);
 
+/* src/sampling.rs:77-230 -- Sampler::sample_with_mask with `r` the first
+ * uniform draw of the rng (sampling.rs:277). mask: one byte per token (1 =
+ * allowed) for tokens < mask_len, tokens >= mask_len allowed; NULL = no mask.
+ * prev: previous output ids. Returns 0 (ok), 1 (EmptyLogits) or 2
+ * (AllTokensMasked). *margin receives the smallest distance, at a float
+ * decision that picked the token (the top-p cut, the multinomial crossing),
+ * between the running sum and its threshold; +INFINITY when there is none.
+ * Ties in the top-p sort, which the reference leaves to sort_unstable, are
+ * broken by descending score, then ascending index. exact = 0 is the reference (f32 running sums);
+ * exact = 1 evaluates the same decisions on the same f32 probabilities with
+ * every sum in double (the softmax normaliser rounded to f32 once): the
+ * exact-arithmetic answer the GPU sampler is held to. */
+int zlo_sample(const float* logits, size_t n, const int64_t* prev, size_t n_prev, float temperature,
+               uint32_t top_k, float top_p, float repetition_penalty, float frequency_penalty,
+               float presence_penalty, const uint8_t* mask, size_t mask_len, float r, int exact,
+               int64_t* token, float* logprob, double* margin);
+
 /* bf16 helpers (round-to-nearest-even), used to feed the oracle exactly the
  * values a bf16 kernel sees. */
 void zlo_f32_to_bf16(const float* src, uint16_t* dst, size_t n);

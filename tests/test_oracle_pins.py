@@ -216,3 +216,92 @@ def test_bf16_round_trip(oracle):
     b = oracle.f32_to_bf16_bits(x)
     assert b.tolist()[:2] == [0x3F80, 0x3F80]  # ties to even
     assert oracle.bf16_bits_to_f32(b)[2] == np.float32(1.0078125)
+
+
+# ---- Sampler (src/sampling.rs:292-659): the reference's tests, run on the
+# restated sampler with many draws r in place of StdRng::seed_from_u64(42).
+
+_RS = [0.001, 0.01, 0.25, 0.5, 0.75, 0.99, 0.999999]
+
+
+def _lin(n):
+    return np.arange(n, dtype=np.float32)
+
+
+def test_sampler_temperature_zero_is_greedy(oracle):
+    for r in _RS:
+        rc, tok, lp, _ = oracle.sample([1.0, 2.0, 3.0, 0.5, 100.0], temperature=0.0, r=r)
+        assert rc == 0 and tok == 4 and lp <= 0.0
+
+
+def test_sampler_temperature_clamp_to_greedy(oracle):
+    rc, tok, _, _ = oracle.sample([1.0, 2.0, 50.0, 0.5], temperature=1e-10)
+    assert rc == 0 and tok == 2
+
+
+def test_sampler_greedy_logprob_is_valid(oracle):
+    x = np.arange(100, dtype=np.float32) * np.float32(0.1)
+    rc, tok, lp, _ = oracle.sample(x, temperature=0.0)
+    assert rc == 0 and lp <= 0.0 and lp >= np.log(np.float32(1.0 / 100))
+
+
+def test_sampler_temperature_scaling_and_top_k_disabled(oracle):
+    for r in _RS:
+        assert oracle.sample(_lin(10), temperature=100.0, r=r)[1] < 10
+        assert oracle.sample(_lin(10), top_k=0, r=r)[1] < 10
+        assert oracle.sample(_lin(10), top_p=1.0, r=r)[1] < 10
+
+
+def test_sampler_top_k(oracle):
+    for r in _RS:
+        assert oracle.sample([0.1, 5.0, 0.2, 3.0], top_k=1, r=r)[1] == 1
+        assert oracle.sample(_lin(100), top_k=3, r=r)[1] >= 97
+
+
+def test_sampler_penalties(oracle):
+    for r in _RS:
+        assert oracle.sample([1.0, 2.0, 100.0, 0.5], prev=[2, 2], r=r)[1] == 2
+        # p = [0.00055, 0.0300, 0.603, 0.366]: token 2 for 0.0306 <= r < 0.634
+        if 0.04 < r < 0.6:
+            assert oracle.sample([1.0, 5.0, 8.0, 7.5], prev=[1], r=r)[1] == 2
+            assert oracle.sample([1.0, 5.0, 8.0, 7.5], prev=[1], repetition_penalty=1.5, r=r)[1] == 2
+        assert oracle.sample([1.0, 100.0, 1.0, 1.0], prev=[1] * 8, frequency_penalty=30.0, r=r)[1] != 1
+        assert oracle.sample([10.0, 15.0, 5.0, 12.0], prev=[1], presence_penalty=10.0, r=r)[1] != 1
+    # penalty arithmetic itself: 5.0 / 1.5 for a positive logit, x * 1.5 for a negative one,
+    # once per occurrence; greedy ignores penalties (the fast path comes first)
+    rc, tok, _, _ = oracle.sample([1.0, 5.0, 8.0, 7.5], prev=[1], repetition_penalty=1.5, top_k=1)
+    assert (rc, tok) == (0, 2)
+    assert oracle.sample([3.0, 2.9], prev=[0, 0], repetition_penalty=1.1, top_k=1)[1] == 1
+    assert oracle.sample([3.0, 2.9], prev=[0, 0], repetition_penalty=1.1, temperature=0.0)[1] == 0
+
+
+def test_sampler_errors(oracle):
+    assert oracle.sample([])[0] == oracle.EMPTY_LOGITS
+    assert oracle.sample([-np.inf] * 10)[0] == oracle.ALL_TOKENS_MASKED
+    assert oracle.sample([1.0, 2.0, 3.0], mask=[0, 0, 0])[0] == oracle.ALL_TOKENS_MASKED
+
+
+def test_sampler_masks(oracle):
+    assert oracle.sample([1.0, 5.0, 3.0, 4.0], mask=[0, 0, 1, 0], temperature=0.0)[1] == 2
+    assert oracle.sample([1.0, 100.0, 2.0, 3.0], mask=[1, 0, 1, 1], top_k=1)[1] == 3
+    assert oracle.sample([1.0, 2.0, 3.0, 4.0, 5.0], mask=[0, 0, 1], temperature=0.0)[1] == 4
+    assert (oracle.sample([1.0, 2.0, 100.0], temperature=0.0)[1]
+            == oracle.sample([1.0, 2.0, 100.0], temperature=0.0, mask=None)[1])
+
+
+def test_sampler_deterministic_and_combined(oracle):
+    a = oracle.sample(_lin(50), temperature=0.8, top_k=10, r=0.3)
+    b = oracle.sample(_lin(50), temperature=0.8, top_k=10, r=0.3)
+    assert a[1] == b[1] and abs(a[2] - b[2]) < 1e-6
+    for r in _RS:
+        rc, tok, lp, _ = oracle.sample(_lin(100), prev=[99, 98, 97], temperature=0.7, top_k=20,
+                                       top_p=0.9, repetition_penalty=1.2, frequency_penalty=0.5,
+                                       presence_penalty=0.3, r=r)
+        assert rc == 0 and tok < 100 and lp <= 0.0
+        assert tok >= 80  # top-k 20 keeps 80..99
+
+
+def test_sampler_multinomial_cdf(oracle):
+    """sample_multinomial (sampling.rs:276-290): the first i with r < cdf(i)."""
+    x = np.log(np.array([0.1, 0.2, 0.3, 0.4], np.float32))
+    assert [oracle.sample(x, r=r)[1] for r in (0.05, 0.15, 0.35, 0.65, 0.95)] == [0, 1, 2, 3, 3]

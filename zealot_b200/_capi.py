@@ -62,6 +62,12 @@ class zl_step_batch(ctypes.Structure):
                 ("max_blocks_per_seq", c_int), ("last_rows", c_void_p), ("num_last", c_int)]
 
 
+class zl_sampling_params(ctypes.Structure):
+    _fields_ = [("temperature", c_float), ("top_k", c_int), ("top_p", c_float),
+                ("repetition_penalty", c_float), ("frequency_penalty", c_float),
+                ("presence_penalty", c_float)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/zealot_attn.h
 SIGNATURES = {
     "zl_ctx_create": (c_int, [P(zl_ctx_cfg), P(c_void_p)]),
@@ -116,6 +122,9 @@ SIGNATURES = {
     "zl_runner_destroy": (c_int, [c_void_p]),
     "zl_runner_step": (c_int, [c_void_p, P(zl_seq_input), c_int, P(c_float)]),
     "zl_runner_drop_state": (c_int, [c_void_p, c_char_p]),
+    "zl_sample": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
+                          c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                          c_void_p]),
     "zl_decoder_step": (c_int, [c_void_p, P(zl_decoder), P(c_void_p), P(c_void_p), c_int64, c_int,
                                 P(zl_step_batch), c_void_p, c_void_p]),
 }

@@ -137,6 +137,7 @@ zl_status zl_ctx_destroy(zl_ctx* ctx) {
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->gather_buf) cudaFree(ctx->gather_buf);
   if (ctx->activations) cudaFree(ctx->activations);
+  if (ctx->sample_scratch) cudaFree(ctx->sample_scratch);
   delete ctx;
   return ZL_OK;
 }

@@ -35,6 +35,9 @@ struct zl_ctx {
   // decoder-step activations (residual stream, q/k/v, attention out, MLP)
   void* activations = nullptr;
   size_t activation_bytes = 0;
+  // sampling rows that do not fit in shared memory
+  void* sample_scratch = nullptr;
+  size_t sample_scratch_bytes = 0;
 };
 
 namespace zl {
