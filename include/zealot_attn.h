@@ -352,16 +352,19 @@ enum {
  * mask_rows [num_rows] (1 = the row is masked) or NULL for every row;
  * penalty_offsets [num_rows+1] into penalty_ids / penalty_counts: the distinct
  * previous output tokens of each row with their occurrence counts (NULL = no
- * history); uniforms [num_rows]: the caller's draw r in [0, 1) per row (the
+ * history); or instead dense_counts [num_rows][vocab] int32, occurrences of
+ * each token in the row's output so far, with update_dense_counts = 1 adding
+ * the sampled token (the history then stays on the device from step to step);
+ * uniforms [num_rows]: the caller's draw r in [0, 1) per row (the
  * reference's rng.gen_range(0.0..1.0), sampling.rs:277); fallback_unmasked:
  * apply the engine's fallback. Outputs token_ids, logprobs, row_status
  * (ZL_SAMPLE_* bits; may be NULL). vocab == 0 is EmptyLogits: ZL_ERR_INVALID_ARG. */
 zl_status zl_sample(zl_ctx* ctx, const float* logits, int num_rows, int64_t vocab,
                     const zl_sampling_params* params, const uint32_t* allowed_bits,
                     const uint8_t* mask_rows, int64_t mask_len, const int32_t* penalty_offsets,
-                    const int64_t* penalty_ids, const int32_t* penalty_counts, const float* uniforms,
-                    int fallback_unmasked, int64_t* token_ids, float* logprobs, int32_t* row_status,
-                    zl_stream stream);
+                    const int64_t* penalty_ids, const int32_t* penalty_counts, int32_t* dense_counts,
+                    int update_dense_counts, const float* uniforms, int fallback_unmasked,
+                    int64_t* token_ids, float* logprobs, int32_t* row_status, zl_stream stream);
 
 /* logits: device fp32 [num_last][vocab]. k_pools / v_pools: host arrays of
  * num_layers device pools, [num_blocks][Hkv][block_size][d] bf16 each.
@@ -369,6 +372,49 @@ zl_status zl_sample(zl_ctx* ctx, const float* logits, int num_rows, int64_t voca
 zl_status zl_decoder_step(zl_ctx* ctx, const zl_decoder* model, void* const* k_pools,
                           void* const* v_pools, int64_t num_blocks, int block_size,
                           const zl_step_batch* batch, float* logits, zl_stream stream);
+
+/* ---------------------------------------------------------------------------
+ * Device-resident decode loop replayed as one CUDA graph. No counterpart in the
+ * reference, whose runner copies block tables, slot mappings and tokens to the
+ * device and the logits back for every sequence of every step
+ * (src/cuda_runner.rs:446,645) and samples on the host (src/engine.rs:153-228).
+ * `rows` decode slots keep on the device their next token, cached length,
+ * block table, sampling parameters and output-token counts. A step is one
+ * graph launch: staging copy (new block ids + draws) -> slots from the device
+ * tables -> zl_decoder_step (decode only) -> zl_sample (next tokens written in
+ * place, counts updated) -> token ids and logprobs copied to pinned host memory.
+ * Block allocation stays with the caller (BlockManager::try_allocate).
+ * ------------------------------------------------------------------------- */
+typedef struct zl_decode_graph zl_decode_graph;
+/* use_graph = 0 issues the same launches eagerly each step (for comparison).
+ * The pools and weights must outlive the graph. Every row starts inactive. */
+zl_status zl_decode_graph_create(zl_ctx* ctx, const zl_decoder* model, void* const* k_pools,
+                                 void* const* v_pools, int64_t num_blocks, int block_size, int rows,
+                                 int max_blocks_per_seq, int use_graph, zl_decode_graph** out);
+zl_status zl_decode_graph_destroy(zl_decode_graph* g);
+/* Row `row` takes a sequence whose first seq_len tokens are in the pools (its
+ * prefill ran through zl_decoder_step): its blocks (host, n_blocks), the token
+ * the next step decodes (at position seq_len), sampling parameters, and its
+ * output history so far (host, for the penalties). Waits for in-flight steps. */
+zl_status zl_decode_graph_set_row(zl_decode_graph* g, int row, const int32_t* block_ids, int n_blocks,
+                                  int seq_len, int64_t next_token, const zl_sampling_params* params,
+                                  const int64_t* history, int n_history);
+/* Makes a row inactive (a finished sequence; its blocks go back to the caller). */
+zl_status zl_decode_graph_clear_row(zl_decode_graph* g, int row);
+/* Rows whose next step writes the first token of a new block (from the host
+ * mirror of the cached lengths; no device read). rows_out has room for `rows`.
+ * ZL_ERR_SEQUENCE_TOO_LONG if a row has no table entry left. */
+zl_status zl_decode_graph_rows_needing_block(const zl_decode_graph* g, int32_t* rows_out, int* n_out);
+/* One step. new_blocks: host [n_new][2] (row, block id), exactly one per row
+ * that needs a block; uniforms: host [rows], the draw r of each row.
+ * Asynchronous on `stream` (NULL: the graph's own stream). */
+zl_status zl_decode_graph_step(zl_decode_graph* g, const int32_t* new_blocks, int n_new,
+                               const float* uniforms, zl_stream stream);
+/* Waits for the last step; copies its tokens [rows] and logprobs [rows]
+ * (optional) to host memory. */
+zl_status zl_decode_graph_tokens(zl_decode_graph* g, int64_t* tokens, float* logprobs);
+/* Kernel nodes in the captured graph (0 when use_graph = 0). */
+int zl_decode_graph_num_kernels(const zl_decode_graph* g);
 
 #ifdef __cplusplus
 }

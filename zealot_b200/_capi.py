@@ -123,8 +123,18 @@ SIGNATURES = {
     "zl_runner_step": (c_int, [c_void_p, P(zl_seq_input), c_int, P(c_float)]),
     "zl_runner_drop_state": (c_int, [c_void_p, c_char_p]),
     "zl_sample": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_int64,
-                          c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
-                          c_void_p]),
+                          c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                          c_void_p, c_void_p, c_void_p]),
+    "zl_decode_graph_create": (c_int, [c_void_p, P(zl_decoder), P(c_void_p), P(c_void_p), c_int64, c_int,
+                                       c_int, c_int, c_int, P(c_void_p)]),
+    "zl_decode_graph_destroy": (c_int, [c_void_p]),
+    "zl_decode_graph_set_row": (c_int, [c_void_p, c_int, P(ctypes.c_int32), c_int, c_int, c_int64,
+                                        P(zl_sampling_params), P(c_int64), c_int]),
+    "zl_decode_graph_clear_row": (c_int, [c_void_p, c_int]),
+    "zl_decode_graph_rows_needing_block": (c_int, [c_void_p, P(ctypes.c_int32), P(c_int)]),
+    "zl_decode_graph_step": (c_int, [c_void_p, P(ctypes.c_int32), c_int, P(c_float), c_void_p]),
+    "zl_decode_graph_tokens": (c_int, [c_void_p, P(c_int64), P(c_float)]),
+    "zl_decode_graph_num_kernels": (c_int, [c_void_p]),
     "zl_decoder_step": (c_int, [c_void_p, P(zl_decoder), P(c_void_p), P(c_void_p), c_int64, c_int,
                                 P(zl_step_batch), c_void_p, c_void_p]),
 }

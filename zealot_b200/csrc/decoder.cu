@@ -34,6 +34,7 @@ struct CublasApi {
   cublasStatus_t (*SetStream)(cublasHandle_t, cudaStream_t) = nullptr;
   cublasStatus_t (*GemmEx)(cublasHandle_t, int, int, int, int, int, const void*, const void*, int, int,
                            const void*, int, int, const void*, void*, int, int, int, int) = nullptr;
+  cublasStatus_t (*SetWorkspace)(cublasHandle_t, void*, size_t) = nullptr;
   bool ok = false;
 };
 
@@ -47,18 +48,32 @@ CublasApi& cublas() {
     a.Destroy = (decltype(a.Destroy))dlsym(h, "cublasDestroy_v2");
     a.SetStream = (decltype(a.SetStream))dlsym(h, "cublasSetStream_v2");
     a.GemmEx = (decltype(a.GemmEx))dlsym(h, "cublasGemmEx");
-    a.ok = a.Create && a.Destroy && a.SetStream && a.GemmEx;
+    a.SetWorkspace = (decltype(a.SetWorkspace))dlsym(h, "cublasSetWorkspace_v2");
+    a.ok = a.Create && a.Destroy && a.SetStream && a.GemmEx && a.SetWorkspace;
   });
   return a;
 }
 
-// One cuBLAS handle per device, created on first use.
+// One cuBLAS handle per device, created on first use, with a workspace of its
+// own so that no GEMM allocates (a step can then be captured in a CUDA graph).
+constexpr size_t kCublasWorkspace = 32u << 20;
 cublasHandle_t cublas_handle(int dev) {
   static cublasHandle_t handles[64] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> g(mu);
   if (dev < 0 || dev >= 64) return nullptr;
-  if (!handles[dev] && cublas().ok) cublas().Create(&handles[dev]);
+  if (!handles[dev] && cublas().ok) {
+    void* ws = nullptr;
+    if (cudaMalloc(&ws, kCublasWorkspace) != cudaSuccess) return nullptr;
+    cublasHandle_t h = nullptr;
+    if (cublas().Create(&h) != 0) { cudaFree(ws); return nullptr; }
+    if (cublas().SetWorkspace(h, ws, kCublasWorkspace) != 0) {
+      cublas().Destroy(h);
+      cudaFree(ws);
+      return nullptr;
+    }
+    handles[dev] = h;  // handle and workspace live until the process exits
+  }
   return handles[dev];
 }
 

@@ -47,6 +47,8 @@ struct SampleArgs {
   const int32_t* pen_off;  // [n+1]
   const int64_t* pen_ids;  // unique in-range token ids per row
   const int32_t* pen_cnt;  // occurrences of each
+  int32_t* dense_counts;   // [n][vocab] occurrences per token (alternative to the lists)
+  int update_counts;       // add the sampled token to dense_counts
   const float* uniforms;   // [n]
   int fallback_unmasked;
   float* scratch;          // [n][vocab] when the row does not fit in shared memory
@@ -242,15 +244,12 @@ __device__ bool sample_row(const SampleArgs& a, const zl_sampling_params& p, int
     for (int64_t i = tid; i < V; i += kThreads) s[i] = __fmul_rn(s[i], inv_t);
     __syncthreads();
   }
-  // 3-5. penalties over the row's unique previous tokens
-  const int pb = a.pen_off ? a.pen_off[row] : 0, pe = a.pen_off ? a.pen_off[row + 1] : 0;
-  if (pe > pb) {
-    const bool fp_on = p.presence_penalty != 0.f || p.frequency_penalty != 0.f;
-    const bool rp_on = p.repetition_penalty != 1.0f;
-    for (int j = pb + tid; j < pe; j += kThreads) {
-      const int64_t id = a.pen_ids[j];
-      if (id < 0 || id >= V) continue;
-      const int c = a.pen_cnt[j];
+  // 3-5. penalties over the row's previous tokens: distinct ids with counts,
+  // or dense per-token counts (a token with count 0 is untouched either way)
+  const bool fp_on = p.presence_penalty != 0.f || p.frequency_penalty != 0.f;
+  const bool rp_on = p.repetition_penalty != 1.0f;
+  if (fp_on || rp_on) {
+    auto penalise = [&](int64_t id, int c) {
       float v = s[id];
       if (fp_on) {
         v = __fsub_rn(v, __fmul_rn((float)c, p.frequency_penalty));
@@ -259,6 +258,18 @@ __device__ bool sample_row(const SampleArgs& a, const zl_sampling_params& p, int
       if (rp_on)
         for (int t = 0; t < c; t++) v = v > 0.f ? __fdiv_rn(v, p.repetition_penalty) : __fmul_rn(v, p.repetition_penalty);
       s[id] = v;
+    };
+    if (a.dense_counts) {
+      const int32_t* cnt = a.dense_counts + (int64_t)row * V;
+      for (int64_t i = tid; i < V; i += kThreads) {
+        const int c = cnt[i];
+        if (c > 0) penalise(i, c);
+      }
+    } else if (a.pen_off) {
+      for (int j = a.pen_off[row] + tid; j < a.pen_off[row + 1]; j += kThreads) {
+        const int64_t id = a.pen_ids[j];
+        if (id >= 0 && id < V) penalise(id, a.pen_cnt[j]);
+      }
     }
     __syncthreads();
   }
@@ -463,6 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(SampleArgs a, int u
   }
   if (threadIdx.x == 0) {
     a.token_ids[row] = token;
+    // the engine appends whatever token it got to output_tokens (engine.rs:219-222)
+    if (a.dense_counts && a.update_counts) a.dense_counts[(int64_t)row * a.vocab + token] += 1;
     a.logprobs[row] = logprob;
     if (a.row_status) a.row_status[row] = status;
   }
@@ -475,7 +488,8 @@ using namespace zl;
 extern "C" zl_status zl_sample(zl_ctx* ctx, const float* logits, int num_rows, int64_t vocab,
                                const zl_sampling_params* params, const uint32_t* allowed_bits,
                                const uint8_t* mask_rows, int64_t mask_len, const int32_t* penalty_offsets,
-                               const int64_t* penalty_ids, const int32_t* penalty_counts, const float* uniforms,
+                               const int64_t* penalty_ids, const int32_t* penalty_counts,
+                               int32_t* dense_counts, int update_dense_counts, const float* uniforms,
                                int fallback_unmasked, int64_t* token_ids, float* logprobs, int32_t* row_status,
                                zl_stream stream) {
   zl_status s = bind_device(ctx);
@@ -489,6 +503,8 @@ extern "C" zl_status zl_sample(zl_ctx* ctx, const float* logits, int num_rows, i
   if (allowed_bits && mask_len < 0) return set_error(ZL_ERR_INVALID_ARG, "sample: mask_len < 0");
   if (penalty_offsets && (!penalty_ids || !penalty_counts))
     return set_error(ZL_ERR_INVALID_ARG, "sample: penalty ids/counts missing");
+  if (penalty_offsets && dense_counts)
+    return set_error(ZL_ERR_INVALID_ARG, "sample: give penalty lists or dense counts, not both");
   SampleArgs a{};
   a.logits = logits;
   a.vocab = vocab;
@@ -500,6 +516,8 @@ extern "C" zl_status zl_sample(zl_ctx* ctx, const float* logits, int num_rows, i
   a.pen_off = penalty_offsets;
   a.pen_ids = penalty_ids;
   a.pen_cnt = penalty_counts;
+  a.dense_counts = dense_counts;
+  a.update_counts = update_dense_counts;
   a.uniforms = uniforms;
   a.fallback_unmasked = fallback_unmasked;
   a.token_ids = token_ids;

@@ -190,3 +190,74 @@ class Decoder:
                                            num_blocks, block_size, ctypes.byref(cb), ptr(logits),
                                            self.ctx.stream(stream)))
         return logits
+
+
+class DecodeGraph:
+    """Device-resident decode loop (zl_decode_graph_*): `rows` decode slots whose
+    tokens, lengths, block tables, sampling parameters and output-token counts
+    stay on the device; one step is one CUDA-graph launch (use_graph=False issues
+    the same launches eagerly). Block ids come from the caller's BlockManager."""
+
+    def __init__(self, dec: Decoder, k_pools, v_pools, block_size: int, rows: int,
+                 max_blocks_per_seq: int, use_graph: bool = True):
+        self.dec, self.ctx, self.rows = dec, dec.ctx, rows
+        self._pools = (list(k_pools), list(v_pools))  # kept alive with the graph
+        L = dec.cfg.num_layers
+        kp = (ctypes.c_void_p * L)(*[ptr(t) for t in k_pools])
+        vp = (ctypes.c_void_p * L)(*[ptr(t) for t in v_pools])
+        h = ctypes.c_void_p()
+        check(self.ctx.lib.zl_decode_graph_create(
+            self.ctx.handle, ctypes.byref(dec._model), kp, vp, k_pools[0].shape[0], block_size, rows,
+            max_blocks_per_seq, int(use_graph), ctypes.byref(h)))
+        self.handle = h
+        self._tok = np.zeros(rows, np.int64)
+        self._lp = np.zeros(rows, np.float32)
+
+    def set_row(self, row: int, block_ids, seq_len: int, next_token: int, params=None, history=()):
+        from .sampling import SamplingParams
+        p = params or SamplingParams()
+        cp = _capi.zl_sampling_params(p.temperature, p.top_k, p.top_p, p.repetition_penalty,
+                                      p.frequency_penalty, p.presence_penalty)
+        b = np.ascontiguousarray(block_ids, np.int32)
+        hist = np.ascontiguousarray(history, np.int64)
+        check(self.ctx.lib.zl_decode_graph_set_row(
+            self.handle, row, b.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), b.size, seq_len,
+            int(next_token), ctypes.byref(cp), hist.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+            hist.size))
+
+    def clear_row(self, row: int):
+        check(self.ctx.lib.zl_decode_graph_clear_row(self.handle, row))
+
+    def rows_needing_block(self) -> list:
+        out = np.zeros(self.rows, np.int32)
+        n = ctypes.c_int()
+        check(self.ctx.lib.zl_decode_graph_rows_needing_block(
+            self.handle, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(n)))
+        return out[: n.value].tolist()
+
+    def step(self, new_blocks: dict, uniforms, stream=None):
+        """new_blocks: {row: block id} for every row in rows_needing_block()."""
+        nb = np.asarray(sorted(new_blocks.items()), np.int32).reshape(-1, 2)
+        u = np.ascontiguousarray(uniforms, np.float32)
+        if u.size != self.rows:
+            raise InvalidArgument(f"need {self.rows} uniforms")
+        check(self.ctx.lib.zl_decode_graph_step(
+            self.handle, nb.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), nb.shape[0],
+            u.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+            0 if stream is None else self.ctx.stream(stream)))
+
+    def tokens(self):
+        """Waits for the last step; (token ids int64 [rows], logprobs float32 [rows])."""
+        check(self.ctx.lib.zl_decode_graph_tokens(
+            self.handle, self._tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+            self._lp.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        return self._tok.copy(), self._lp.copy()
+
+    @property
+    def num_kernels(self) -> int:
+        return int(self.ctx.lib.zl_decode_graph_num_kernels(self.handle))
+
+    def close(self):
+        if self.handle:
+            check(self.ctx.lib.zl_decode_graph_destroy(self.handle))
+            self.handle = None

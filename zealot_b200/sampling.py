@@ -106,8 +106,11 @@ class GpuSampler:
         return SamplerBatch(rows, vocab, d_params, d_bits, d_rows, mask_len, d_off, d_ids, d_cnt)
 
     def launch(self, batch: SamplerBatch, logits, uniforms, out: SampledTokens = None,
-               fallback_unmasked: bool = True, stream=None) -> SampledTokens:
-        """One zl_sample launch over prepared inputs; uniforms: float32 device [rows]."""
+               fallback_unmasked: bool = True, dense_counts=None, update_counts: bool = False,
+               stream=None) -> SampledTokens:
+        """One zl_sample launch over prepared inputs; uniforms: float32 device [rows].
+        dense_counts: int32 device [rows][vocab] output-token counts used for the
+        penalties instead of the prepared lists; update_counts adds each sampled token."""
         import torch
         if (logits.dtype != torch.float32 or logits.dim() != 2 or not logits.is_contiguous()
                 or tuple(logits.shape) != (batch.rows, batch.vocab)):
@@ -120,7 +123,8 @@ class GpuSampler:
         check(self.ctx.lib.zl_sample(
             self.ctx.handle, ptr(logits), batch.rows, batch.vocab, ptr(batch.params),
             ptr(batch.allowed_bits), ptr(batch.mask_rows), batch.mask_len, ptr(batch.pen_off),
-            ptr(batch.pen_ids), ptr(batch.pen_cnt), ptr(uniforms), int(fallback_unmasked),
+            ptr(batch.pen_ids), ptr(batch.pen_cnt), ptr(dense_counts), int(update_counts),
+            ptr(uniforms), int(fallback_unmasked),
             ptr(out.token_ids), ptr(out.logprobs), ptr(out.status), self.ctx.stream(stream)))
         return out
 
