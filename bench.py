@@ -615,6 +615,83 @@ def run_c4(args):
     ctx.close()
 
 
+def run_decode_loop(args):
+    """--workload decode-loop: steady-state decode steps of the Mistral-7B-shaped
+    decoder through the device-resident loop (zl_decode_graph), replayed as a
+    CUDA graph and, for comparison, as the same launches issued eagerly.
+    Rows 32 and 248 (contexts U{1024..8192}, random bf16 KV and weights); a step
+    = block bookkeeping on the host, staging copy, 32 layers, sampling, token
+    ids back to pinned host memory. tokens/s = active rows / step time."""
+    import torch
+    import zealot_b200 as zb
+    from zealot_b200.decoder import Decoder, DecoderConfig, DecodeGraph, random_weights
+    from zealot_b200.sampling import SamplingParams as SP
+    torch.cuda.set_device(0)
+    cfg = DecoderConfig.mistral_7b()
+    rng = np.random.default_rng(505)
+    R = 248
+    steps, warm = args.steps, args.warmup
+    lens = rng.integers(1024, 8193, size=R).astype(np.int32)
+    extra = (steps + warm) * 2 + 4  # every row runs all steps of both modes and both sizes
+    mb = int((lens.max() + extra * 2 + BS - 1) // BS) + 1
+    nblk = int(((lens + BS - 1) // BS).sum()) + R * (extra * 2 // BS + 2)
+    w = random_weights(cfg, seed=505)
+    g = torch.Generator(device="cuda").manual_seed(505)
+    shape = (nblk, cfg.num_kv_heads, BS, cfg.head_dim)
+    kps = [torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) for _ in range(cfg.num_layers)]
+    vps = [torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) for _ in range(cfg.num_layers)]
+    ctx = zb.GpuContext(0)
+    dec = Decoder(ctx, cfg, w)
+    stream = torch.cuda.Stream(0)
+    kinds = [SP(temperature=0.0), SP(temperature=0.7, top_k=50, top_p=0.9), SP(top_p=0.95, repetition_penalty=1.1)]
+    res = {}
+    for rows in (32, R):
+        for use_graph in (True, False):
+            perm = list(rng.permutation(nblk))
+            dg = DecodeGraph(dec, kps, vps, BS, rows=rows, max_blocks_per_seq=mb, use_graph=use_graph)
+            for r in range(rows):
+                nb = (int(lens[r]) + BS - 1) // BS
+                dg.set_row(r, [int(perm.pop()) for _ in range(nb)], int(lens[r]),
+                           int(rng.integers(0, cfg.vocab)), kinds[r % 3],
+                           history=list(rng.integers(0, cfg.vocab, 32)))
+
+            def one():
+                dg.step({r: int(perm.pop()) for r in dg.rows_needing_block()},
+                        rng.random(rows).astype(np.float32), stream=stream)
+
+            for _ in range(warm):
+                one()
+            dg.tokens()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            e0.record(stream)
+            for _ in range(steps):
+                one()
+            e1.record(stream)
+            host_s = (time.perf_counter() - t0) / steps
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            dg.tokens()
+            ctx.check_status(stream.cuda_stream)
+            key = f"rows{rows}_{'graph' if use_graph else 'eager'}"
+            res[key] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(rows / (ms * 1e-3), 1),
+                        "host_us_per_step": round(host_s * 1e6, 1)}
+            if use_graph:
+                res[key]["graph_kernel_nodes"] = dg.num_kernels
+            dg.close()
+    line = {"metric": "decode_loop_tokens_per_s", "value": res[f"rows{R}_graph"]["tokens_per_s"],
+            "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+            "ms_per_step": res[f"rows{R}_graph"]["ms_per_step"], "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (seeded random bf16 weights and KV)",
+            "config": {"workload": "steady-state decode of a Mistral-7B-shaped decoder (32 layers) through "
+                                   "zl_decode_graph: rows with contexts U[1024,8192], greedy / top-k+top-p / "
+                                   "top-p+repetition sampling; inputs larger than L2"},
+            "modes": res}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -715,9 +792,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-side", action="store_true", help="skip the prefill / cache side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "c5", "prefill", "cache", "c4"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "c5", "prefill", "cache", "c4", "decode-loop"],
+                    default="decode",
                     help="decode (C2, the headline), c5 (long-context decode), a single side kernel "
-                         "on its C3 workload, or c4 (a full Mistral-7B-shaped engine step, 1 GPU)")
+                         "on its C3 workload, c4 (a full Mistral-7B-shaped engine step, 1 GPU) or "
+                         "decode-loop (its steady-state decode through the CUDA-graph loop, 1 GPU)")
     ap.add_argument("--lite", action="store_true",
                     help="only warm-up + timed steps of the kernel (no clock soak, e2e, side runs or "
                          "CPU baseline): the form used under ncu")
@@ -739,10 +818,10 @@ def main():
     if args.workload in ("prefill", "cache"):
         run_side_only(args)
         return
-    if args.workload == "c4":
+    if args.workload in ("c4", "decode-loop"):
         if world > 1:
-            raise SystemExit("--workload c4 runs on one GPU")
-        run_c4(args)
+            raise SystemExit(f"--workload {args.workload} runs on one GPU")
+        (run_c4 if args.workload == "c4" else run_decode_loop)(args)
         return
     if args.workload == "c5":
         args.no_side = True

@@ -71,6 +71,7 @@ def lib():
         L.zlo_sample.argtypes = [_f32p, _sz, _i64p, _sz, _f, ctypes.c_uint32, _f, _f, _f, _f, _u8p, _sz,
                                  _f, ctypes.c_int, _i64p, _f32p, ctypes.POINTER(ctypes.c_double)]
         L.zlo_sample.restype = ctypes.c_int
+        L.zlo_softmax_probs.argtypes = [_f32p, _f32p, _sz]
         _lib = L
     return _lib
 
@@ -257,6 +258,14 @@ def argmax(x) -> int:
     """src/sampling.rs:233-243: first maximum wins."""
     x = _f32(x).reshape(-1)
     return int(lib().zlo_argmax(_p(x, _f32p), x.size))
+
+
+def softmax(scores) -> np.ndarray:
+    """src/sampling.rs:254-273."""
+    x = _f32(scores).reshape(-1)
+    out = np.empty_like(x)
+    lib().zlo_softmax_probs(_p(x, _f32p), _p(out, _f32p), x.size)
+    return out
 
 
 EMPTY_LOGITS, ALL_TOKENS_MASKED = 1, 2  # SamplingError (src/sampling.rs:15-20)

@@ -456,6 +456,8 @@ static void zlo_softmax(const float* s, float* p, size_t n, int exact) {
     for (size_t i = 0; i < n; i++) p[i] /= sum;
 }
 
+void zlo_softmax_probs(const float* scores, float* probs, size_t n) { zlo_softmax(scores, probs, n, 0); }
+
 int zlo_sample(const float* logits, size_t n, const int64_t* prev, size_t n_prev, float temperature,
                uint32_t top_k, float top_p, float repetition_penalty, float frequency_penalty,
                float presence_penalty, const uint8_t* mask, size_t mask_len, float r, int exact,

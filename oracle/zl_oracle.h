@@ -124,6 +124,9 @@ int zlo_prefill_varlen_rows(const float* q, const float* k, const float* v,
 /* src/sampling.rs:233-243 -- argmax, first maximum wins. */
 int64_t zlo_argmax(const float* x, size_t n);
 
+/* src/sampling.rs:254-273 -- softmax over finite scores (max-subtracted). */
+void zlo_softmax_probs(const float* scores, float* probs, size_t n);
+
 /* src/sampling.rs:77-230 -- Sampler::sample_with_mask with `r` the first
  * uniform draw of the rng (sampling.rs:277). mask: one byte per token (1 =
  * allowed) for tokens < mask_len, tokens >= mask_len allowed; NULL = no mask.

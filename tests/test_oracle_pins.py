@@ -305,3 +305,11 @@ def test_sampler_multinomial_cdf(oracle):
     """sample_multinomial (sampling.rs:276-290): the first i with r < cdf(i)."""
     x = np.log(np.array([0.1, 0.2, 0.3, 0.4], np.float32))
     assert [oracle.sample(x, r=r)[1] for r in (0.05, 0.15, 0.35, 0.65, 0.95)] == [0, 1, 2, 3, 3]
+
+
+def test_sampler_softmax(oracle):
+    """softmax_sums_to_one and softmax_stable_with_extreme_values (sampling.rs:620-645)."""
+    p = oracle.softmax([1.0, 2.0, 3.0, 4.0, 5.0])
+    assert abs(float(np.sum(p, dtype=np.float32)) - 1.0) < 1e-5
+    p = oracle.softmax([1e5, -1e5, 0.0, 5e4])
+    assert abs(float(np.sum(p, dtype=np.float32)) - 1.0) < 1e-5 and np.isfinite(p).all()
