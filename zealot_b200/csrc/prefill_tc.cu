@@ -16,6 +16,9 @@
 // O += P V straight from TMEM. The MMA warp interleaves the two heads
 // (PV0(j), S0(j+1), PV1(j), S1(j+1)) so one warpgroup's softmax overlaps the
 // other's matrix products. Causal tiles past the diagonal are never loaded.
+// The softmax is bound by instruction issue as much as by the MUFU unit, so
+// its arithmetic runs on packed fp32 pairs (FFMA2/FADD2, three-input max) and
+// one exponential in eight runs on the FMA pipe instead of MUFU.
 // Every mbarrier wait is bounded (status word + unwind instead of a hang).
 #include "zl_internal.h"
 #include "zl_ptx.cuh"
@@ -71,6 +74,21 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
 // covers keys 16kk..16kk+15; the two 64-dim boxes are LBO = 16 KB apart.
 __device__ __forceinline__ uint64_t desc_v(uint32_t tile, int kk) {
   return sdesc(tile + kk * 2048, HALF, 1024, 2);
+}
+
+// 2^x on the FMA and integer pipes, for the share of the softmax exponentials
+// taken off the MUFU unit: x = j + f with j = rint(x) (adding 1.5 * 2^23 leaves
+// j in the low mantissa bits) and f in [-0.5, 0.5]; 2^f by a cubic fitted to 2^f
+// on that interval (reweighted least squares, max relative error 7.5e-5, well
+// under the bf16 rounding of P); j is added to the exponent field. x is clamped
+// at -125 so the exponent stays normal (2^-125 ~ 2e-38 is zero for every use
+// here).
+__device__ __forceinline__ float ex2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05517166f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -227,7 +245,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         } else {
 #pragma unroll
           for (int i = 0; i < 32; i++)
-            mx8[i & 7] = fmaxf(mx8[i & 7], fmaxf(__uint_as_float(va[i]), __uint_as_float(vb[i])));
+            mx8[i & 7] = max3(mx8[i & 7], __uint_as_float(va[i]), __uint_as_float(vb[i]));
         }
       }
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
@@ -238,9 +256,11 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
       const float m_new = grow ? fmaxf(m, m_tile) : m;
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_use);
-      float ls8[8];
+      // four pair accumulators for the row sum; x = s * scale - m as fp32 pairs
+      uint64_t ls2[4];
 #pragma unroll
-      for (int u = 0; u < 8; u++) ls8[u] = 0.f;
+      for (int u = 0; u < 4; u++) ls2[u] = 0ull;
+      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(-m_use, -m_use);
 #pragma unroll
       for (int hh = 0; hh < 2; hh++) {
         tmem_ld32(tSr + 64 * hh, va);
@@ -250,17 +270,18 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
         for (int i = 0; i < 16; i++) {
           const int k0 = 64 * hh + 2 * i, k1 = k0 + 32;
-          float p0 = ex2(__uint_as_float(va[2 * i]) * sc - m_use);
-          float p1 = ex2(__uint_as_float(va[2 * i + 1]) * sc - m_use);
-          float p2 = ex2(__uint_as_float(vb[2 * i]) * sc - m_use);
-          float p3 = ex2(__uint_as_float(vb[2 * i + 1]) * sc - m_use);
-          if (edge) {
+          const float2 xa = f2_unpack(f2_fma(f2_pack(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1])), sc2, nm2));
+          const float2 xb = f2_unpack(f2_fma(f2_pack(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1])), sc2, nm2));
+          float p0 = ex2(xa.x), p1 = ex2(xa.y), p2 = ex2(xb.x);
+          float p3 = (i & 1) ? ex2_fma(xb.y) : ex2(xb.y);
+          if (edge) {  // masked keys: 0 (the FMA form would give 2^-125 for -inf)
             p0 = k0 < key_lim ? p0 : 0.f;
             p1 = k0 + 1 < key_lim ? p1 : 0.f;
             p2 = k1 < key_lim ? p2 : 0.f;
             p3 = k1 + 1 < key_lim ? p3 : 0.f;
           }
-          ls8[i & 7] += (p0 + p1) + (p2 + p3);
+          ls2[(2 * i) & 3] = f2_add(ls2[(2 * i) & 3], f2_pack(p0, p1));
+          ls2[(2 * i + 1) & 3] = f2_add(ls2[(2 * i + 1) & 3], f2_pack(p2, p3));
           pa[i] = pack_bf16x2(p0, p1);
           pb[i] = pack_bf16x2(p2, p3);
         }
@@ -268,6 +289,13 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         // all below the S columns still to be read
         tmem_st16(tSr + 32 * hh, pa);
         tmem_st16(tSr + 32 * hh + 16, pb);
+      }
+      float ls8[8];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float2 v = f2_unpack(ls2[u]);
+        ls8[2 * u] = v.x;
+        ls8[2 * u + 1] = v.y;
       }
       const float lsum = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       l = l * alpha + lsum;
