@@ -267,18 +267,30 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     locate(f0, b, kvh, j);
     bool neg = false;
     const int32_t* tb = tables + (int64_t)b * a.max_blocks;
-    for (int t = lane; t < j; t += 32) neg |= (tb[t] < 0);
+    // eight independent loads per lane in flight: one memory latency for the
+    // first 256 entries instead of one per 32
+    for (int t0 = 0; t0 < j; t0 += 256) {
+      int v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int t = t0 + 32 * u + lane;
+        v[u] = t < j ? __ldg(tb + t) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) neg |= v[u] < 0;
+    }
     carry_trunc = __any_sync(0xffffffffu, neg) ? 1 : 0;
     carry_seg = b * Hkv + kvh;
   }
   auto build_chunk = [&](int base) {
     const int idx = base + lane;
     const bool ok = idx < nwork;
-    int seg = -1, e = 0, b = 0, kvh = 0, j = 0;
+    int seg = -1, e = 0, b = 0, kvh = 0, j = 0, len = 0;
     if (ok) {
       locate(f0 + idx, b, kvh, j);
       seg = b * Hkv + kvh;
       e = tables[(int64_t)b * a.max_blocks + j];
+      len = a.seq_lens[b];  // issued with the table read: one latency, not two
     }
     const unsigned negm = __ballot_sync(0xffffffffu, ok && e < 0);
     const int prev = __shfl_up_sync(0xffffffffu, seg, 1);
@@ -293,7 +305,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         atomicOr(a.status, ZL_DEV_OOB);
       } else {
         const int nb = prefix[b + 1] - prefix[b];
-        nv = (j == nb - 1) ? (a.seq_lens[b] - j * BS) : BS;
+        nv = (j == nb - 1) ? (len - j * BS) : BS;
         y = (int)(((int64_t)e * Hkv + kvh) * BS);
       }
     }
@@ -354,6 +366,10 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   constexpr float kLazy = 8.f;
   bool timed_out = false;
 
+  // q of the warp's next segment, loaded while the current one streams
+  uint32_t qn[8][2];
+  int qn_seg = -1;
+
   int i = 0;
   while (i < nwork && !timed_out) {
     // ----- segment (cb, ckvh) starting at block cj
@@ -367,15 +383,33 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     const int head0 = ckvh * G;
 
     // q fragments (B operand of S^T = K q^T): head n = quad, d pairs
-    uint32_t qf[8][2];
-    {
-      const bool hv = quad < G;
+    const bool hv = quad < G;
+    auto load_q = [&](int qb, int qh0, uint32_t (&dst)[8][2]) {
       const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-          a.q + ((int64_t)cb * a.H + head0 + (hv ? quad : 0)) * D);
+          a.q + ((int64_t)qb * a.H + qh0 + (hv ? quad : 0)) * D);
 #pragma unroll
       for (int ks = 0; ks < 8; ks++) {
-        qf[ks][0] = hv ? __ldg(qrow + ks * 8 + qid) : 0u;
-        qf[ks][1] = hv ? __ldg(qrow + ks * 8 + 4 + qid) : 0u;
+        dst[ks][0] = hv ? __ldg(qrow + ks * 8 + qid) : 0u;
+        dst[ks][1] = hv ? __ldg(qrow + ks * 8 + 4 + qid) : 0u;
+      }
+    };
+    uint32_t qf[8][2];
+    if (qn_seg == cb * Hkv + ckvh) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ks++) { qf[ks][0] = qn[ks][0]; qf[ks][1] = qn[ks][1]; }
+    } else {
+      load_q(cb, head0, qf);
+    }
+    qn_seg = -1;
+    if (seg_E < f1) {  // the range continues into the next non-empty segment
+      int nbq = cb, nkq = ckvh + 1;
+      if (nkq == Hkv) {
+        nkq = 0;
+        do { nbq++; } while (nbq < B && prefix[nbq + 1] == prefix[nbq]);
+      }
+      if (nbq < B) {
+        load_q(nbq, nkq * G, qn);
+        qn_seg = nbq * Hkv + nkq;
       }
     }
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
@@ -562,11 +596,31 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
           const int64_t fc = (int64_t)c * TB / W;
           return a.partials + 2 * c + ((c == wa && fc < seg_S) ? 1 : 0);
         };
-        // (1) per-head max and weights: lane i handles contributors i, i+32, ...
-        float M[MAX_G], den[MAX_G];
+        // Lane c holds contributor c's (m, l) for every head; the rows of
+        // contributors 0 and 1 are loaded in the same round, so a split of
+        // up to two contributors costs one L2 round trip before the math.
+        float M[MAX_G], den[MAX_G], mc[MAX_G], lc[MAX_G];
+        float4 x1[MAX_G], x2[MAX_G];
+        {
+          const bool mine = lane < nc;
+          const Partial* pc = slot_of(wa + (mine ? lane : 0));
+          const float4* o1 = reinterpret_cast<const float4*>(&slot_of(wa)->o[0][0]) + lane;
+          const float4* o2 = reinterpret_cast<const float4*>(&slot_of(wa + (nc > 1 ? 1 : 0))->o[0][0]) + lane;
 #pragma unroll
-        for (int n = 0; n < MAX_G; n++) { M[n] = -INFINITY; den[n] = 0.f; }
-        for (int c0 = 0; c0 < nc; c0 += 32)
+          for (int n = 0; n < MAX_G; n++) {
+            mc[n] = -INFINITY;
+            lc[n] = 0.f;
+            if (n < G) {
+              if (mine) { mc[n] = __ldcg(&pc->m[n]); lc[n] = __ldcg(&pc->l[n]); }
+              x1[n] = __ldcg(o1 + n * (D / 4));
+              x2[n] = __ldcg(o2 + n * (D / 4));
+            }
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < MAX_G; n++) { M[n] = mc[n]; den[n] = 0.f; }
+        // contributors past 32 (very long sequences): their maxima too
+        for (int c0 = 32; c0 < nc; c0 += 32)
           if (c0 + lane < nc) {
             const Partial* pc = slot_of(wa + c0 + lane);
 #pragma unroll
@@ -577,8 +631,6 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         for (int n = 0; n < MAX_G; n++)
 #pragma unroll
           for (int off = 16; off; off >>= 1) M[n] = fmaxf(M[n], __shfl_xor_sync(0xffffffffu, M[n], off));
-        // (2) weighted sum of the o rows: every contributor's rows of all heads
-        // are loaded together (independent L2 reads), two contributors at a time
         float4 num[MAX_G];
 #pragma unroll
         for (int n = 0; n < MAX_G; n++) num[n] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -590,9 +642,10 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
             for (int n = 0; n < MAX_G; n++) {
               wl[n] = 0.f;
               if (n < G) {
-                const float mc = __ldcg(&pc->m[n]);
-                wl[n] = (mc == -INFINITY) ? 0.f : __expf(mc - M[n]);
-                den[n] += wl[n] * __ldcg(&pc->l[n]);
+                const float m_ = c0 == 0 ? mc[n] : __ldcg(&pc->m[n]);
+                const float l_ = c0 == 0 ? lc[n] : __ldcg(&pc->l[n]);
+                wl[n] = (m_ == -INFINITY) ? 0.f : __expf(m_ - M[n]);
+                den[n] += wl[n] * l_;
               }
             }
           } else {
@@ -602,14 +655,15 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
           const int cnt = min(32, nc - c0);
           for (int k = 0; k < cnt; k += 2) {
             const bool second = k + 1 < cnt;
-            const float4* o1 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k)->o[0][0]) + lane;
-            const float4* o2 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k + (second ? 1 : 0))->o[0][0]) + lane;
-            float4 x1[MAX_G], x2[MAX_G];
+            if (c0 + k > 0) {  // rows of contributors 0 and 1 are already loaded
+              const float4* o1 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k)->o[0][0]) + lane;
+              const float4* o2 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k + (second ? 1 : 0))->o[0][0]) + lane;
 #pragma unroll
-            for (int n = 0; n < MAX_G; n++) {
-              if (n < G) {
-                x1[n] = __ldcg(o1 + n * (D / 4));
-                x2[n] = __ldcg(o2 + n * (D / 4));
+              for (int n = 0; n < MAX_G; n++) {
+                if (n < G) {
+                  x1[n] = __ldcg(o1 + n * (D / 4));
+                  x2[n] = __ldcg(o2 + n * (D / 4));
+                }
               }
             }
 #pragma unroll
