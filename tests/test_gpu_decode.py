@@ -65,6 +65,22 @@ def test_bf16_long_context_split(ctx, oracle):
         assert np.max(np.abs(got - ref)) <= BF16_ATOL
 
 
+def test_bf16_ragged_many_segments(ctx, oracle):
+    """Short and mid-length sequences mixed (48 sequences, 1 to 2600 tokens): most warp
+    ranges cross several (sequence, kv head) segments, whole ones and split ones; one
+    sequence ends early at a negative table entry."""
+    rng = np.random.default_rng(8)
+    H, Hkv, d, bs = 32, 8, 128, 16
+    lens = np.concatenate([rng.integers(1, 48, size=24), rng.integers(200, 2600, size=24)])
+    rng.shuffle(lens)
+    nblk = int(((lens + bs - 1) // bs).sum())
+    q, kp, vp, table, lens = decode_case(rng, len(lens), lens, H, Hkv, d, bs, nblk + 16)
+    table[int(np.argmax(lens)), 3] = -1
+    for _ in range(2):  # twice: the workspace counters must come back to zero
+        got, ref = _run_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs)
+        assert np.max(np.abs(got - ref)) <= BF16_ATOL
+
+
 def test_bf16_c2_full(ctx, oracle):
     """Config C2 at full size: B=64, 32/8 heads, d=128, ctx U[512, 4096], block tables a
     seeded random permutation of a 65536-block pool. The pools are drawn on the GPU; the
