@@ -299,6 +299,8 @@ typedef struct {
   const void* w_gate_up;  /* [2*inter][hidden]: gate rows, then up rows       */
   const void* w_down;     /* [hidden][inter]                                  */
 } zl_layer_weights;
+/* When wk starts where wq ends and wv where wk ends (one [(H+2*Hkv)*d][hidden]
+ * buffer), steps of at most 256 rows compute q, k and v with one GEMM. */
 
 typedef struct {
   int num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate;

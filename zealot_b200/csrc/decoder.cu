@@ -172,6 +172,30 @@ __global__ void silu_mul_bf16_kernel(const __nv_bfloat16* __restrict__ gu, int64
   }
 }
 
+// y[t] = [q | k | v] rows of one fused projection -> q[t][nq], k[t][nk], v[t][nk]
+// (16-byte chunks; nq, nk multiples of 8).
+__global__ void split_qkv_bf16_kernel(const __nv_bfloat16* __restrict__ y, int64_t T, int nq, int nk,
+                                      __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
+                                      __nv_bfloat16* __restrict__ v) {
+  const int64_t row = (nq + 2 * nk) / 8;  // chunks per fused row
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < T * row;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / row;
+    const int c = (int)(i - t * row);
+    const uint4 val = reinterpret_cast<const uint4*>(y)[i];
+    if (c < nq / 8) reinterpret_cast<uint4*>(q + t * nq)[c] = val;
+    else if (c < (nq + nk) / 8) reinterpret_cast<uint4*>(k + t * nk)[c - nq / 8] = val;
+    else reinterpret_cast<uint4*>(v + t * nk)[c - (nq + nk) / 8] = val;
+  }
+}
+
+// Steps with at most this many rows read wq, wk and wv with one GEMM when they are
+// stored back to back: a few rows make the projections weight-read-bound, and
+// the 1024-wide k and v products alone reach only a small part of HBM
+// bandwidth. The fused product goes to the gate/up buffer (free at that point
+// of the layer) and a copy kernel splits it.
+constexpr int64_t kFusedQkvRows = 256;
+
 unsigned grid_of(int64_t work, int num_sms) {
   int64_t g = (work + 255) / 256;
   const int64_t cap = (int64_t)num_sms * 16;
@@ -242,10 +266,20 @@ extern "C" zl_status zl_decoder_step(zl_ctx* ctx, const zl_decoder* m, void* con
     rmsnorm_bf16_kernel<<<(unsigned)T, 256, 0, st>>>(x, nullptr, (const __nv_bfloat16*)L.attn_norm, hid,
                                                       m->rms_eps, h);
     ZL_LAUNCH_CHECK(ctx);
-    if ((s = linear(hb, st, h, L.wq, q, T, (int64_t)H * d, hid, false)) ||
-        (s = linear(hb, st, h, L.wk, k, T, (int64_t)Hkv * d, hid, false)) ||
-        (s = linear(hb, st, h, L.wv, v, T, (int64_t)Hkv * d, hid, false)))
+    const int64_t nq = (int64_t)H * d, nk = (int64_t)Hkv * d;
+    const bool fused = T <= kFusedQkvRows && d % 8 == 0 && 2 * (int64_t)I >= nq + 2 * nk &&
+                       (const uint8_t*)L.wk == (const uint8_t*)L.wq + nq * hid * e &&
+                       (const uint8_t*)L.wv == (const uint8_t*)L.wk + nk * hid * e;
+    if (fused) {
+      if ((s = linear(hb, st, h, L.wq, gu, T, nq + 2 * nk, hid, false))) return s;
+      split_qkv_bf16_kernel<<<grid_of(T * (nq + 2 * nk) / 8, ctx->num_sms), 256, 0, st>>>(
+          gu, T, (int)nq, (int)nk, q, k, v);
+      ZL_LAUNCH_CHECK(ctx);
+    } else if ((s = linear(hb, st, h, L.wq, q, T, nq, hid, false)) ||
+               (s = linear(hb, st, h, L.wk, k, T, nk, hid, false)) ||
+               (s = linear(hb, st, h, L.wv, v, T, nk, hid, false))) {
       return s;
+    }
     if ((s = zl_reshape_and_cache(ctx, k, v, k_pools[l], v_pools[l], b->slot_mapping, T, Hkv, d, block_size,
                                   num_blocks, ZL_BF16, stream)))
       return s;

@@ -62,8 +62,13 @@ def random_weights(cfg: DecoderConfig, seed: int = 0, device: str = "cuda", std:
 
     layers = []
     for _ in range(cfg.num_layers):
-        layers.append({k: (norm(s[0]) if len(s) == 1 else mat(*s))
-                       for k, s in cfg.layer_shapes().items()})
+        lw = {k: (norm(s[0]) if len(s) == 1 else mat(*s)) for k, s in cfg.layer_shapes().items()}
+        # q, k and v projections back to back in one buffer (row slices of it): a step
+        # with few rows then reads the three with one GEMM (zl_decoder_step)
+        qkv = torch.cat([lw["wq"], lw["wk"], lw["wv"]])
+        nq, nk = lw["wq"].shape[0], lw["wk"].shape[0]
+        lw["wq"], lw["wk"], lw["wv"] = qkv[:nq], qkv[nq:nq + nk], qkv[nq + nk:]
+        layers.append(lw)
     return {"embed": mat(cfg.vocab, cfg.hidden) * 50, "layers": layers,
             "final_norm": norm(cfg.hidden), "lm_head": mat(cfg.vocab, cfg.hidden)}
 
