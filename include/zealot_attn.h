@@ -109,7 +109,8 @@ zl_status zl_reshape_and_cache(zl_ctx* ctx, const void* k /*device*/, const void
  * negative entries ending a sequence, seq_lens [B]) plus the pool size for
  * bounds checks, the softmax scale (<= 0 means 1/sqrt(d)), the head mapping
  * and the split-KV count (0 = automatic). q, pools and out share `dtype`.
- * An empty context writes zeros. */
+ * An empty context writes zeros. head_dim up to 256; larger head dims return
+ * ZL_ERR_UNSUPPORTED. */
 zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const void* v_pool,
                           const int32_t* block_tables, const int32_t* seq_lens, void* out,
                           int num_seqs, int num_heads, int num_kv_heads, int head_dim,
@@ -170,7 +171,8 @@ zl_status zl_merge_partials(zl_ctx* ctx, const float* m, const float* l, const f
  * (the row count of the buffers, which bounds every tile load); max_seq_len
  * bounds the launch. causal != 0 masks keys after the query. bf16 with
  * head_dim 128 and an even GQA group runs on the tcgen05/TMEM tensor-core
- * kernel; other shapes on the CUDA-core kernel. */
+ * kernel; other shapes on the CUDA-core kernel, head_dim up to 256 (larger:
+ * ZL_ERR_UNSUPPORTED). */
 zl_status zl_prefill_varlen(zl_ctx* ctx, const void* q, const void* k, const void* v,
                             const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
                             int64_t total_tokens, void* out,
