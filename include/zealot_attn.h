@@ -84,6 +84,14 @@ int zl_abi_version(void);
 zl_status zl_check_status(zl_ctx* ctx, zl_stream stream);
 /* Number of kernels this context has launched (for launch accounting). */
 uint64_t zl_launch_count(const zl_ctx* ctx);
+/* Diagnostic, no counterpart in the reference: one warp waits on a barrier that
+ * nothing completes, the way every kernel of this library waits on its
+ * barriers; the bounded wait gives up after about a second, sets the timeout
+ * bit of the status word and returns, and a second wait in the same warp then
+ * gives up at once. The next zl_check_status reports ZL_ERR_TIMEOUT and clears
+ * the word; the context stays usable. Exercises the timeout path without
+ * faulting or hanging the GPU. Costs about one second of GPU time. */
+zl_status zl_selftest_wait_timeout(zl_ctx* ctx, zl_stream stream);
 
 /* ------------------------------------------------------- reshape_and_cache */
 

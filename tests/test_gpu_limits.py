@@ -9,6 +9,8 @@
 - bf16 shapes outside the tensor-core / fast paths (odd GQA group, head_dim 64,
   more than 8 query heads per kv head) fall back to the generic kernels and
   still match the oracle within the bf16 tolerance (2e-2 absolute).
+- A device wait that nothing satisfies ends on its own budget and is reported as
+  DeviceTimeout (failure detection without a GPU fault).
 """
 import numpy as np
 import pytest
@@ -134,3 +136,24 @@ def test_bf16_prefill_outside_tensor_core_path(ctx, oracle, H, Hkv, d):
     ctx.check_status()
     ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=True, num_threads=8)
     assert np.max(np.abs(to_f32(out) - ref)) <= BF16_ATOL
+
+
+def test_bounded_wait_times_out_and_context_recovers(ctx, oracle):
+    """A device wait that nothing satisfies gives up on its own budget (about a
+    second), flags the status word (DeviceTimeout on the host) and leaves the
+    context usable: no trap, no hang."""
+    import time
+    import zealot_b200 as zb
+    from zealot_b200.errors import check
+    ctx.check_status()
+    t0 = time.perf_counter()
+    check(ctx.lib.zl_selftest_wait_timeout(ctx.handle, ctx.stream()))
+    with pytest.raises(zb.DeviceTimeout):
+        ctx.check_status()
+    assert 0.05 < time.perf_counter() - t0 < 60
+    ctx.check_status()  # the word was cleared by the first read
+    rng = np.random.default_rng(12)
+    H, Hkv, d, bs = 8, 2, 128, 16
+    q, kp, vp, table, lens = decode_case(rng, 3, [7, 99, 700], H, Hkv, d, bs, 64)
+    got, ref = _decode_bf16(ctx, oracle, q, kp, vp, table, lens, H, Hkv, d, bs)
+    assert np.max(np.abs(got - ref)) <= BF16_ATOL

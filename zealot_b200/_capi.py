@@ -77,6 +77,7 @@ SIGNATURES = {
     "zl_abi_version": (c_int, []),
     "zl_check_status": (c_int, [c_void_p, c_void_p]),
     "zl_launch_count": (c_uint64, [c_void_p]),
+    "zl_selftest_wait_timeout": (c_int, [c_void_p, c_void_p]),
     "zl_reshape_and_cache": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_int64, c_int, c_int, c_int, c_int64, c_int, c_void_p]),
     "zl_paged_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

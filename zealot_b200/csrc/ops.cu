@@ -1,6 +1,7 @@
 // ops.cu -- argument checking and kernel selection for the attention entry
 // points of include/zealot_attn.h.
 #include "zl_internal.h"
+#include "zl_ptx.cuh"
 
 using namespace zl;
 
@@ -14,9 +15,34 @@ zl_status check_heads(int H, int Hkv, int d, const char* who) {
   return ZL_OK;
 }
 
+// One warp waits on an mbarrier whose phase never completes (count 1, no
+// arrival): the bounded wait times out and flags the status word, then a
+// second wait returns at once because the flag is set. Both waits end on their
+// own; nothing traps.
+__global__ void selftest_wait_timeout_kernel(int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = zl::ptx::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    zl::ptx::mbar_init(b, 1);
+    zl::ptx::fence_mbar_init();
+  }
+  __syncwarp();
+  (void)zl::ptx::mbar_wait_warp(b, 0, status);  // gives up after the wait budget
+  (void)zl::ptx::mbar_wait_warp(b, 0, status);  // gives up at once: the status says timed out
+}
+
 }  // namespace
 
 extern "C" {
+
+zl_status zl_selftest_wait_timeout(zl_ctx* ctx, zl_stream stream) {
+  zl_status s = bind_device(ctx);
+  if (s != ZL_OK) return s;
+  selftest_wait_timeout_kernel<<<1, 32, 0, S(stream)>>>(ctx->d_status);
+  ZL_LAUNCH_CHECK(ctx);
+  return ZL_OK;
+}
+
 
 zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const void* v_pool,
                           const int32_t* block_tables, const int32_t* seq_lens, void* out,
