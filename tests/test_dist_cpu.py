@@ -109,3 +109,54 @@ def test_gloo_two_ranks(oracle, mode):
     full = oracle.paged_decode(q, kp, vp, table, lens, H, Hkv, d, bs, nb)
     for r in range(2):
         np.testing.assert_allclose(outs[r], full, rtol=1e-5, atol=1e-6)
+
+
+def _watch_worker(rank, port, scenario, q_out):
+    sys.path.insert(0, ROOT)
+    import datetime
+    import time
+    import torch.distributed as dist
+    from zealot_b200.dist import PeerWatch
+    from zealot_b200.errors import PeerLost
+    store = dist.TCPStore("127.0.0.1", port, 2, is_master=(rank == 0),
+                          timeout=datetime.timedelta(seconds=30))
+    w = PeerWatch(store, rank, 2, timeout_s=1.0)
+    res, t0 = [], time.monotonic()
+    try:
+        for n in range(3):
+            if rank == 1 and n == 2:  # rank 1 stops between steps 1 and 2
+                if scenario == "leave":
+                    w.leave()
+                break
+            w.step(n)
+            res.append(n)
+    except PeerLost as e:
+        res.append(f"PeerLost: {e}")
+    q_out.put((rank, res, time.monotonic() - t0))
+    if rank == 0:
+        time.sleep(0.5)  # the store lives in rank 0: let rank 1 finish with it
+
+
+@pytest.mark.parametrize("scenario", ["leave", "crash"])
+def test_peer_watch_reports_a_rank_gone_between_steps(scenario):
+    """Two ranks (processes) step together; rank 1 stops after step 1, announcing it
+    (leave) or not (crash). Rank 0 learns it on the host at step 2 -- at once, or
+    after its 1 s deadline -- as PeerLost, before it would launch anything."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    qo = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_watch_worker, args=(r, port, scenario, qo)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outs = {r: (res, dt) for r, res, dt in (qo.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert outs[1][0] == [0, 1]
+    res0 = outs[0][0]
+    assert res0[:2] == [0, 1] and len(res0) == 3 and res0[2].startswith("PeerLost: rank 1")
+    if scenario == "leave":
+        assert "left the job after step 1" in res0[2]
+    else:
+        assert "did not reach step 2 within 1 s" in res0[2]

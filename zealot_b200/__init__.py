@@ -18,7 +18,7 @@ runs in the library. Importing fails loudly if the library is not built.
 from . import _capi
 from .errors import (ZealotError, InternalError, OutOfBlocks, StaleHandle, BlockNotAllocated,
                      InvalidBlockSize, SequenceTooLong, CudaError, OobBlockError, DeviceTimeout,
-                     NcclError, Unsupported, InvalidArgument)
+                     NcclError, PeerLost, Unsupported, InvalidArgument)
 from .context import GpuContext, GQA_GROUPED, GQA_MODULO
 from .attention import CudaAttention
 from .kv_cache import BlockManager, BlockHandle, KVCache
@@ -30,6 +30,6 @@ __all__ = [
     "GpuContext", "CudaAttention", "BlockManager", "BlockHandle", "KVCache", "CudaModelRunner",
     "Sequence", "StepOut", "ZealotError", "InternalError", "OutOfBlocks", "StaleHandle",
     "BlockNotAllocated", "InvalidBlockSize", "SequenceTooLong", "CudaError", "OobBlockError",
-    "DeviceTimeout", "NcclError", "Unsupported", "InvalidArgument", "GQA_GROUPED", "GQA_MODULO",
+    "DeviceTimeout", "NcclError", "PeerLost", "Unsupported", "InvalidArgument", "GQA_GROUPED", "GQA_MODULO",
     "lib",
 ]

@@ -17,11 +17,12 @@ src/bin/zealot-backend.rs:317); this module has no counterpart there.
 from __future__ import annotations
 
 import ctypes
+import time
 
 import numpy as np
 
 from .context import GpuContext, GQA_GROUPED, dtype_code, ptr
-from .errors import check, InvalidArgument
+from .errors import check, InvalidArgument, PeerLost
 
 
 def kv_head_group(rank: int, world: int, num_kv_heads: int) -> tuple[int, int]:
@@ -57,14 +58,80 @@ def token_split(seq_lens, rank: int, world: int, block_size: int):
     return begin.astype(np.int32), end.astype(np.int32)
 
 
+class PeerWatch:
+    """Host-side liveness of the ranks of a multi-GPU job, through the job's
+    key-value store (torch.distributed's TCPStore or any object with set / get /
+    check). Before every collective step each rank publishes the step it is about
+    to run and waits, up to `timeout_s`, until every peer has published it too.
+    A peer that left (leave()) or stopped between steps is reported as PeerLost
+    before this rank launches anything for the step, so no collective is ever
+    left waiting on the GPU for a rank that is gone."""
+
+    LEFT = "left:"  # + the last step the rank reached: peers still pass steps up to it
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, prefix: str = "zl/peer/"):
+        if world <= 0 or not 0 <= rank < world or timeout_s <= 0:
+            raise InvalidArgument(f"rank {rank} of {world}, timeout {timeout_s}")
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+        self.last = -1
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}{r}"
+
+    def _read(self, r: int) -> str | None:
+        key = self._key(r)
+        if not self.store.check([key]):
+            return None
+        v = self.store.get(key)
+        return v.decode() if isinstance(v, (bytes, bytearray)) else str(v)
+
+    def step(self, n: int) -> None:
+        """Returns once every peer has reached step n; raises PeerLost otherwise."""
+        try:
+            self.store.set(self._key(self.rank), str(n))
+            self.last = n
+            deadline = time.monotonic() + self.timeout_s
+            for peer in range(self.world):
+                if peer == self.rank:
+                    continue
+                while True:
+                    v = self._read(peer)
+                    if v is not None and v.startswith(self.LEFT):
+                        gone_after = int(v[len(self.LEFT):])
+                        if gone_after >= n:
+                            break
+                        raise PeerLost(f"rank {peer} left the job after step {gone_after}, before step {n}")
+                    if v is not None and int(v) >= n:
+                        break
+                    if time.monotonic() > deadline:
+                        raise PeerLost(f"rank {peer} did not reach step {n} within {self.timeout_s:g} s "
+                                       f"(last at step {v})")
+                    time.sleep(0.002)
+        except PeerLost:
+            raise
+        except Exception as e:  # the store itself is gone with the rank that hosted it
+            raise PeerLost(f"the job's store stopped answering at step {n}: {e}") from e
+
+    def leave(self) -> None:
+        """Tells the peers that this rank is gone (their next step() raises at once)."""
+        try:
+            self.store.set(self._key(self.rank), f"{self.LEFT}{self.last}")
+        except Exception:
+            pass
+
+
 class SequenceSplitDecoder:
     """Decode for sequences whose KV is split across GPUs: local partial triples,
     NCCL all-gather over NVLink, merge kernel. One instance per process/GPU."""
 
-    def __init__(self, ctx: GpuContext, rank: int, world: int, broadcast_id):
+    def __init__(self, ctx: GpuContext, rank: int, world: int, broadcast_id, watch: PeerWatch | None = None):
         """`broadcast_id(bytes_or_None) -> bytes` shares rank 0's 128-byte NCCL id
-        (e.g. via torch.distributed.broadcast_object_list)."""
+        (e.g. via torch.distributed.broadcast_object_list). With `watch`, every
+        decode() first checks that all ranks reached the same step (PeerLost
+        otherwise) before it launches the partial decode and the NCCL merge."""
         self.ctx, self.lib, self.rank, self.world = ctx, ctx.lib, rank, world
+        self.watch, self._step = watch, 0
         buf = (ctypes.c_uint8 * 128)()
         if rank == 0:
             check(self.lib.zl_nccl_get_unique_id(buf))
@@ -79,6 +146,9 @@ class SequenceSplitDecoder:
                num_blocks: int | None = None, scale: float = 0.0, gqa_map: int = GQA_GROUPED,
                stream=None) -> None:
         import torch
+        if self.watch is not None:
+            self.watch.step(self._step)
+            self._step += 1
         B = tok_end.numel()
         m = torch.empty((B, num_heads), dtype=torch.float32, device=q.device)
         l = torch.empty_like(m)
@@ -95,3 +165,5 @@ class SequenceSplitDecoder:
 
     def close(self) -> None:
         check(self.lib.zl_nccl_finalize(self.ctx.handle))
+        if self.watch is not None:
+            self.watch.leave()

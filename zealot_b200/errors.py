@@ -31,6 +31,11 @@ class NcclError(ZealotError):
     status = 5
 
 
+class PeerLost(NcclError):
+    """A peer rank left the job or stopped answering; found on the host before
+    any collective of the step was launched (dist.PeerWatch)."""
+
+
 class Unsupported(ZealotError):
     status = 6
 
