@@ -136,14 +136,19 @@ zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const 
  * used. Its split-KV scratch is a static device array of about 5.4 MB that
  * every GPU which loads the library holds until the process exits. Limits:
  * num_seqs <= 4096 and num_seqs * num_kv_heads <= 16384, else
- * ZL_ERR_INVALID_ARG; other shapes return ZL_ERR_UNSUPPORTED. The first call
- * on a device resolves the array's device address and sets the kernel's
- * shared-memory limit, so make that first call before any stream capture.
- * All calls share the array: calls whose kernels overlap on the GPU race and
- * give wrong results; calls ordered on one stream are safe. status (device,
- * optional, caller-cleared): the kernel ORs 1 (block id outside the pool)
- * and 2 (a bounded wait ran out) into it; while bit 2 is set the kernel
- * returns without work. */
+ * ZL_ERR_INVALID_ARG; other shapes return ZL_ERR_UNSUPPORTED. Every call
+ * looks up the array's device address (no allocation); the first call on a
+ * device also sets the kernel's shared-memory limit, so make that first call
+ * before any stream capture. Do not carry the library across a device reset
+ * without calling it again outside a capture. All calls share the array:
+ * calls whose kernels overlap on the GPU race and give wrong results; calls
+ * ordered on one stream are safe.
+ * status (device int, required, cleared by the caller): the return code only
+ * says the kernel was queued. The kernel ORs 1 (a block id or seq_len outside
+ * the pool or table: that access was skipped) and 2 (a bounded wait ran out)
+ * into *status. While bit 2 is set a call still returns ZL_OK but its kernel
+ * does no work and leaves `out` as it was. So read and clear *status after
+ * every call (or every step) before trusting `out`. */
 zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, const void* v_pool,
                                   const int32_t* block_tables, const int32_t* seq_lens, void* out,
                                   int* status, int num_seqs, int num_heads, int num_kv_heads,
@@ -193,11 +198,31 @@ zl_status zl_prefill_varlen(zl_ctx* ctx, const void* q, const void* k, const voi
  * link-time NCCL dependency. No reference counterpart (the reference has no
  * multi-GPU code); these carry the north-star sequence-split merge. */
 zl_status zl_nccl_get_unique_id(uint8_t id_out[128]);
-zl_status zl_nccl_init(zl_ctx* ctx, const uint8_t id[128], int nranks, int rank);
+/* Creates a non-blocking communicator (every rank calls it with the same id)
+ * and sizes the gather buffer once for steps of up to max_rows rows of up to
+ * max_head_dim: nranks * max_rows * (2 + max_head_dim) fp32 of device memory.
+ * timeout_ms bounds every later wait on a collective (creation gets ten times
+ * that); a collective not finished by then means a peer is gone. */
+zl_status zl_nccl_init(zl_ctx* ctx, const uint8_t id[128], int nranks, int rank, int64_t max_rows,
+                       int max_head_dim, int timeout_ms);
 /* All-gathers every rank's partial triple (m, l [rows], o [rows][d] fp32,
- * device) into the context workspace and merges them into out [rows][d]. */
+ * device) into the gather buffer and merges them into out [rows][d].
+ * Asynchronous; allocates nothing. rows / head_dim beyond the sizes given to
+ * zl_nccl_init: ZL_ERR_INVALID_ARG. After an abort: ZL_ERR_NCCL. */
 zl_status zl_nccl_merge(zl_ctx* ctx, const float* m, const float* l, const float* o,
                         int64_t rows, int head_dim, void* out, zl_dtype dtype, zl_stream stream);
+/* Waits up to timeout_ms (<= 0: the zl_nccl_init timeout) for the last
+ * merge's all-gather. If it does not finish in time, or NCCL reports an
+ * asynchronous error, the communicator is aborted (its kernels stop) and
+ * ZL_ERR_TIMEOUT / ZL_ERR_NCCL is returned; the context stays usable for
+ * single-GPU calls. zl_check_status does the same wait before it synchronises
+ * its stream. */
+zl_status zl_nccl_wait(zl_ctx* ctx, int timeout_ms);
+/* Aborts the communicator at once (e.g. when the host learns that a peer is
+ * gone); later zl_nccl_merge calls return ZL_ERR_NCCL. */
+zl_status zl_nccl_abort(zl_ctx* ctx);
+/* Destroys the communicator (aborting it if a collective cannot finish) and
+ * frees the gather buffer. */
 zl_status zl_nccl_finalize(zl_ctx* ctx);
 
 /* ------------------------------------------------------------ block manager */
@@ -425,6 +450,9 @@ zl_status zl_decode_graph_step(zl_decode_graph* g, const int32_t* new_blocks, in
 /* Waits for the last step; copies its tokens [rows] and logprobs [rows]
  * (optional) to host memory. */
 zl_status zl_decode_graph_tokens(zl_decode_graph* g, int64_t* tokens, float* logprobs);
+/* Waits for the last step; copies the logits it sampled from, host
+ * [rows][vocab] fp32 (before temperature, penalties and masks). */
+zl_status zl_decode_graph_logits(zl_decode_graph* g, float* logits);
 /* Kernel nodes in the captured graph (0 when use_graph = 0). */
 int zl_decode_graph_num_kernels(const zl_decode_graph* g);
 

@@ -165,37 +165,96 @@ def test_oob_block_id_is_reported(ctx, oracle, dtype):
     ctx.check_status()  # the status word was cleared by the first read
 
 
-def test_partial_and_merge(ctx, oracle):
-    """Sequence split: partial triples over two token ranges merge to the full decode."""
+def _check_triple(m, l, o, rm, rl, ro, bf16):
+    """Partial triple against the oracle. m is the true maximum score, so it
+    matches to fp32 rounding; l sums fp32 probabilities; o is compared after
+    normalisation (o / l), with the bf16 tolerance on the bf16 path where the
+    probabilities enter the P.V product rounded to bf16."""
+    np.testing.assert_allclose(m, rm, rtol=0, atol=1e-4)
+    np.testing.assert_allclose(l, rl, rtol=1e-4, atol=1e-30)
+    empty = rl == 0
+    assert np.all(o[empty] == 0) and np.all(np.isneginf(m[empty]))
+    den = np.where(empty, 1.0, rl)[..., None]
+    err = float(np.max(np.abs(o / np.where(empty, 1.0, l)[..., None] - ro / den)))
+    assert err <= (BF16_ATOL if bf16 else F32_RTOL), err
+
+
+def _partial_ranges(ctx, oracle, q, kp, vp, table, lens, cuts, H, Hkv, d, bs, dtype):
+    """Runs paged_forward_partial over consecutive ranges [cuts[i], cuts[i+1]) of every
+    sequence, checks each triple against the oracle and returns the merged output."""
     import torch
     import zealot_b200 as zb
-    rng = np.random.default_rng(10)
-    B, H, Hkv, d, bs = 4, 8, 2, 128, 16
-    q, kp, vp, table, lens = decode_case(rng, B, [50, 300, 16, 1000], H, Hkv, d, bs, 256)
     attn = zb.CudaAttention(ctx)
-    tq, q32 = bf16_tensor(oracle, q)
-    tk, k32 = bf16_tensor(oracle, kp)
-    tv, v32 = bf16_tensor(oracle, vp)
+    bf16 = dtype == "bf16"
+    if bf16:
+        tq, q32 = bf16_tensor(oracle, q)
+        tk, k32 = bf16_tensor(oracle, kp)
+        tv, v32 = bf16_tensor(oracle, vp)
+    else:
+        (tq, tk, tv), (q32, k32, v32) = (f32_tensor(q), f32_tensor(kp), f32_tensor(vp)), (q, kp, vp)
     tt = torch.from_numpy(table).cuda()
-    cut = np.array([20, 150, 0, 999], np.int32)
-    zeros = np.zeros(B, np.int32)
+    B = table.shape[0]
     ms, ls, os_ = [], [], []
-    for lo, hi in ((zeros, cut), (cut, lens)):
-        m = torch.empty((B, H), dtype=torch.float32, device="cuda")
-        l = torch.empty_like(m)
-        o = torch.empty((B, H, d), dtype=torch.float32, device="cuda")
+    for lo, hi in zip(cuts[:-1], cuts[1:]):
+        lo, hi = np.asarray(lo, np.int32), np.asarray(hi, np.int32)
+        m = torch.full((B, H), float("nan"), dtype=torch.float32, device="cuda")
+        l = torch.full_like(m, float("nan"))
+        o = torch.full((B, H, d), float("nan"), dtype=torch.float32, device="cuda")
         attn.paged_forward_partial(tq, tk, tv, tt, torch.from_numpy(lo).cuda(), torch.from_numpy(hi).cuda(),
-                                   m, l, o, B, H, Hkv, d, bs, table.shape[1])
+                                   m, l, o, B, H, Hkv, d, bs, table.shape[1], num_blocks=kp.shape[0])
+        ctx.check_status()
         rm, rl, ro = oracle.paged_decode_partial(q32, k32, v32, table, lo, hi, H, Hkv, d, bs, kp.shape[0])
-        np.testing.assert_allclose(m.cpu().numpy(), rm, rtol=1e-5, atol=1e-5)
-        np.testing.assert_allclose(l.cpu().numpy(), rl, rtol=1e-4)
-        np.testing.assert_allclose(o.cpu().numpy(), ro, rtol=1e-4, atol=1e-3)
+        _check_triple(m.cpu().numpy(), l.cpu().numpy(), o.cpu().numpy(), rm, rl, ro, bf16)
         ms.append(m); ls.append(l); os_.append(o)
     out = torch.empty((B, H, d), dtype=torch.float32, device="cuda")
     attn.merge_partials(torch.stack(ms), torch.stack(ls), torch.stack(os_), out)
     ctx.check_status()
-    full = oracle.paged_decode(q32, k32, v32, table, lens, H, Hkv, d, bs, kp.shape[0])
-    assert rel_err(out.cpu().numpy(), full) <= 1e-4
+    full = oracle.paged_decode(q32, k32, v32, table, lens, H, Hkv, d, bs, kp.shape[0], num_threads=8)
+    return out.cpu().numpy(), full
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_partial_and_merge(ctx, oracle, dtype):
+    """Sequence split: partial triples over two token ranges merge to the full decode.
+    bf16 runs the fast kernel's partial form, fp32 the CUDA-core kernel."""
+    rng = np.random.default_rng(10)
+    B, H, Hkv, d, bs = 4, 8, 2, 128, 16
+    q, kp, vp, table, lens = decode_case(rng, B, [50, 300, 16, 1000], H, Hkv, d, bs, 256)
+    cut = np.array([20, 150, 0, 999], np.int32)
+    got, full = _partial_ranges(ctx, oracle, q, kp, vp, table, lens, [np.zeros(B, np.int32), cut, lens],
+                                H, Hkv, d, bs, dtype)
+    if dtype == "f32":
+        assert rel_err(got, full) <= F32_RTOL
+    else:
+        assert np.max(np.abs(got - full)) <= BF16_ATOL
+
+
+def test_bf16_partial_ragged_ranges(ctx, oracle):
+    """Partial form of the fast kernel: range starts inside a block, empty ranges,
+    ranges past a sentinel, sequences long enough that each range splits over many
+    warps (last-arriver merge) -- three ranges per sequence merged back."""
+    rng = np.random.default_rng(21)
+    B, H, Hkv, d, bs = 7, 32, 8, 128, 16
+    lens = np.array([0, 5, 300, 1000, 17001, 40000, 2600], np.int32)
+    q, kp, vp, table, lens = decode_case(rng, B, lens, H, Hkv, d, bs, 4096)
+    table[6, 100] = -1  # sequence 6 ends after 1600 tokens
+    c1 = np.array([0, 3, 7, 333, 4097, 20001, 1590], np.int32)
+    c2 = np.array([0, 5, 300, 334, 9000, 20002, 2000], np.int32)
+    got, full = _partial_ranges(ctx, oracle, q, kp, vp, table, lens,
+                                [np.zeros(B, np.int32), c1, c2, lens], H, Hkv, d, bs, "bf16")
+    assert np.max(np.abs(got - full)) <= BF16_ATOL
+
+
+def test_bf16_partial_one_kv_head_long(ctx, oracle):
+    """One kv head over 131072-token ranges: every range spreads over hundreds of
+    warps, so the partial form's grid-barrier merge runs."""
+    rng = np.random.default_rng(22)
+    B, H, Hkv, d, bs, L = 2, 8, 1, 128, 16, 131072
+    q, kp, vp, table, lens = decode_case(rng, B, [L, L - 9], H, Hkv, d, bs, 2 * L // bs)
+    mid = np.array([65536 + 8, 1000], np.int32)
+    got, full = _partial_ranges(ctx, oracle, q, kp, vp, table, lens,
+                                [np.zeros(B, np.int32), mid, lens], H, Hkv, d, bs, "bf16")
+    assert np.max(np.abs(got - full)) <= BF16_ATOL
 
 
 def test_bf16_c5_long_context(ctx, oracle):

@@ -3,7 +3,12 @@
 1. Against a host-managed loop built from the same parts (StepBatch.build ->
    zl_decoder_step -> zl_sample with host penalty lists, blocks allocated on the
    host): identical tokens, logprobs and pool bytes after 40 steps that cross
-   block boundaries, with greedy, top-k, top-p and penalty rows.
+   block boundaries, with greedy, top-k, top-p and penalty rows. At four of the
+   steps the graph's logits are also checked against the plain PyTorch fp32
+   restatement of the layer loop (test_gpu_decoder.reference_step) run on fp32
+   copies of the same pools, within the decoder test's tolerance, so the
+   replayed steps are tied to an independent reference, not only to the same
+   kernels issued from the host.
 2. The captured graph against the same launches issued eagerly, with an
    inactive row and a row recycled mid-run: identical tokens.
 3. Host-side errors: a missing or unexpected block.
@@ -17,12 +22,13 @@ BS = 16
 MAXB = 16
 
 
-def _setup(ctx, seed=3):
+def _setup(ctx, seed=3, with_weights=False):
     from test_gpu_decoder import _cfg
     from zealot_b200.decoder import Decoder, random_weights
     cfg = _cfg(layers=2)
-    dec = Decoder(ctx, cfg, random_weights(cfg, seed=seed))
-    return cfg, dec
+    w = random_weights(cfg, seed=seed)
+    dec = Decoder(ctx, cfg, w)
+    return (cfg, dec, w) if with_weights else (cfg, dec)
 
 
 def _prefill(dec, prompts, tables, pools):
@@ -41,7 +47,8 @@ def test_decode_graph_matches_host_loop(ctx):
     import torch
     from zealot_b200.decoder import DecodeGraph, StepBatch
     from zealot_b200.sampling import GpuSampler
-    cfg, dec = _setup(ctx)
+    from test_gpu_decoder import reference_step
+    cfg, dec, w = _setup(ctx, with_weights=True)
     rng = np.random.default_rng(0)
     lens0 = [30, 47, 16, 5]
     prompts = [rng.integers(0, cfg.vocab, n) for n in lens0]
@@ -83,12 +90,32 @@ def test_decode_graph_matches_host_loop(ctx):
     assert g.num_kernels > 4 * cfg.num_layers
     for r in range(4):
         g.set_row(r, tables[r], lens0[r], int(first[r]), params[r], history=[int(first[r])])
+    tabs_b, lens_b, toks_b = [list(t) for t in tables], list(lens0), first.copy()
+    checked = 0
     for t in range(40):
         need = g.rows_needing_block()
-        g.step({r: int(free_b.pop()) for r in need}, draws[t])
+        new = {r: int(free_b.pop()) for r in need}
+        for r, blk in new.items():
+            tabs_b[r].append(blk)
+        lens_b = [n + 1 for n in lens_b]
+        anchor = t in (0, 15, 16, 39)
+        if anchor:  # fp32 copies of the pools as this step finds them
+            k32 = [p.float() for p in pools_b[0]]
+            v32 = [p.float() for p in pools_b[1]]
+        g.step(new, draws[t])
         tok, lp = g.tokens()
         assert (tok == want_tok[t]).all(), (t, tok, want_tok[t])
         np.testing.assert_array_equal(lp, want_lp[t])
+        if anchor:
+            dt = np.full((4, MAXB), -1, np.int32)
+            for r in range(4):
+                dt[r, : len(tabs_b[r])] = tabs_b[r]
+            ref = reference_step(cfg, w, StepBatch.build([], toks_b, dt, lens_b, [], BS), k32, v32,
+                                 round_bf16=True)
+            torch.testing.assert_close(torch.from_numpy(g.logits()), ref.cpu(), atol=2e-2, rtol=2e-2)
+            checked += 1
+        toks_b = tok
+    assert checked == 4
     ctx.check_status()
     for l in range(cfg.num_layers):
         assert torch.equal(pools_a[0][l], pools_b[0][l]) and torch.equal(pools_a[1][l], pools_b[1][l])

@@ -84,3 +84,46 @@ def test_bf16_prefill_c3_sampled(ctx, oracle):
     ref = oracle.prefill_varlen_rows(q32, k32, v32, cu, rows, H, Hkv, d, causal=True, num_threads=8)
     got = out.float().cpu().numpy()[rows]
     assert np.max(np.abs(got - ref)) <= 2e-2
+
+
+@pytest.mark.parametrize("path", ["tcgen05", "generic"])
+@pytest.mark.parametrize("bad", ["past_end", "backwards", "longer_than_max"])
+def test_malformed_cu_seqlens_is_reported(ctx, oracle, path, bad):
+    """cu_seqlens lives in device memory, so the kernels check it: a sequence that
+    ends past total_tokens, runs backwards, or is longer than max_seq_len is
+    skipped and reported (ZL_ERR_OOB_BLOCK from check_status). `out` is the head of
+    a larger buffer whose tail is a guard region: it must come back untouched, and
+    the well-formed sequence before the bad one must still match the oracle."""
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = (32, 8, 128) if path == "tcgen05" else (4, 2, 64)
+    T, guard = 300, 256
+    rng = np.random.default_rng(91)
+    _, q, k, v = _case(rng, [T], H, Hkv, d)
+    good = 120
+    cu, max_len = {
+        "past_end": (np.array([0, good, T + 40], np.int32), 256),
+        "backwards": (np.array([0, good, good - 7], np.int32), 256),
+        "longer_than_max": (np.array([0, good, T], np.int32), 128),
+    }[bad]
+    if path == "tcgen05":
+        (tq, q32), (tk, k32), (tv, v32) = (bf16_tensor(oracle, x) for x in (q, k, v))
+        dt, tol = torch.bfloat16, 2e-2
+    else:
+        tq, tk, tv, q32, k32, v32 = f32_tensor(q), f32_tensor(k), f32_tensor(v), q, k, v
+        dt, tol = torch.float32, 1e-4
+    out_full = torch.full((T + guard, H, d), 7.0, dtype=dt, device="cuda")
+    out = out_full[:T]
+    zb.CudaAttention(ctx).forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d, max_len,
+                                      causal=True)
+    with pytest.raises(zb.OobBlockError):
+        ctx.check_status()
+    assert torch.all(out_full[T:] == 7.0), "a store left the caller's buffer"
+    ref = oracle.prefill_varlen(q32[:good], k32[:good], v32[:good], np.array([0, good], np.int32), H, Hkv, d,
+                                causal=True, num_threads=8)
+    got = to_f32(out)[:good]
+    if path == "tcgen05":
+        assert np.max(np.abs(got - ref)) <= tol
+    else:
+        for r in range(good):
+            assert rel_err(got[r], ref[r]) <= tol

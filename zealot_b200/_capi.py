@@ -1,7 +1,7 @@
 """ctypes binding of include/zealot_attn.h (libzealot_attn.so).
 
 This is the Python twin of the `extern "C"` block a Rust host would write
-(see INTEGRATION.md). It loads the in-tree library and declares every entry
+for the same header. It loads the in-tree library and declares every entry
 point; nothing here computes.
 """
 from __future__ import annotations
@@ -96,9 +96,11 @@ SIGNATURES = {
                                   c_int64, c_void_p, c_int, c_int, c_int, c_float, c_int, c_int,
                                   c_int, c_void_p]),
     "zl_nccl_get_unique_id": (c_int, [c_void_p]),
-    "zl_nccl_init": (c_int, [c_void_p, c_void_p, c_int, c_int]),
+    "zl_nccl_init": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int64, c_int, c_int]),
     "zl_nccl_merge": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
                               c_int, c_void_p]),
+    "zl_nccl_wait": (c_int, [c_void_p, c_int]),
+    "zl_nccl_abort": (c_int, [c_void_p]),
     "zl_nccl_finalize": (c_int, [c_void_p]),
     "zl_block_manager_create": (c_int, [c_uint64, c_uint64, P(c_void_p)]),
     "zl_block_manager_destroy": (c_int, [c_void_p]),
@@ -135,6 +137,7 @@ SIGNATURES = {
     "zl_decode_graph_rows_needing_block": (c_int, [c_void_p, P(ctypes.c_int32), P(c_int)]),
     "zl_decode_graph_step": (c_int, [c_void_p, P(ctypes.c_int32), c_int, P(c_float), c_void_p]),
     "zl_decode_graph_tokens": (c_int, [c_void_p, P(c_int64), P(c_float)]),
+    "zl_decode_graph_logits": (c_int, [c_void_p, P(c_float)]),
     "zl_decode_graph_num_kernels": (c_int, [c_void_p]),
     "zl_decoder_step": (c_int, [c_void_p, P(zl_decoder), P(c_void_p), P(c_void_p), c_int64, c_int,
                                 P(zl_step_batch), c_void_p, c_void_p]),

@@ -130,12 +130,13 @@ zl_status zl_nccl_finalize(zl_ctx* ctx);
 zl_status zl_ctx_destroy(zl_ctx* ctx) {
   if (!ctx) return ZL_OK;
   cudaSetDevice(ctx->device);
+  // First the communicator: a collective whose peer is gone is aborted (bounded
+  // wait) instead of blocking the device synchronisation below for good.
+  if (ctx->nccl_comm || ctx->gather_buf || ctx->nccl_done) zl_nccl_finalize(ctx);
   cudaDeviceSynchronize();
-  if (ctx->nccl_comm) zl_nccl_finalize(ctx);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->counters) cudaFree(ctx->counters);
-  if (ctx->gather_buf) cudaFree(ctx->gather_buf);
   if (ctx->activations) cudaFree(ctx->activations);
   if (ctx->sample_scratch) cudaFree(ctx->sample_scratch);
   delete ctx;
@@ -145,6 +146,10 @@ zl_status zl_ctx_destroy(zl_ctx* ctx) {
 zl_status zl_check_status(zl_ctx* ctx, zl_stream stream) {
   zl_status s = bind_device(ctx);
   if (s != ZL_OK) return s;
+  // A pending sequence-split all-gather is waited for with a deadline first, so
+  // a lost peer turns into ZL_ERR_TIMEOUT here rather than a stream that never
+  // drains.
+  if ((s = nccl_wait_pending(ctx, ctx->nccl_timeout_ms)) != ZL_OK) return s;
   ZL_CUDA_TRY(cudaStreamSynchronize(S(stream)));
   int h = 0;
   ZL_CUDA_TRY(cudaMemcpy(&h, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));

@@ -175,12 +175,20 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
 prefill_generic_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                        const int32_t* __restrict__ cu_seqlens, T* __restrict__ out, int H, int Hkv,
-                       int d, float scale, int causal, int gqa_modulo) {
+                       int d, float scale, int causal, int gqa_modulo, int64_t total_tokens,
+                       int* status) {
   __shared__ AttendShared sh;
   // grid: x = row within the sequence, y = head, z = sequence
   const int64_t i = blockIdx.x;
   const int h = blockIdx.y;
   const int64_t start = cu_seqlens[blockIdx.z], end = cu_seqlens[blockIdx.z + 1];
+  // A sequence outside [0, total_tokens], running backwards, or longer than the
+  // launch's rows (gridDim.x = max_seq_len) is reported and skipped: no access
+  // leaves the caller's buffers.
+  if (start < 0 || end < start || end > total_tokens || end - start > (int64_t)gridDim.x) {
+    if (threadIdx.x == 0 && i == 0) atomicOr(status, ZL_DEV_OOB);
+    return;
+  }
   if (start + i >= end) return;
   const int tid = threadIdx.x;
   const int64_t row = start + i;
@@ -258,8 +266,8 @@ zl_status launch_decode_generic(zl_ctx* ctx, const void* q, const void* k_pool, 
 
 zl_status launch_prefill_generic(zl_ctx* ctx, const void* q, const void* k, const void* v,
                                  const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
-                                 void* out, int H, int Hkv, int d, float scale, int causal,
-                                 zl_gqa_map map, zl_dtype dtype, cudaStream_t st) {
+                                 int64_t total_tokens, void* out, int H, int Hkv, int d, float scale,
+                                 int causal, zl_gqa_map map, zl_dtype dtype, cudaStream_t st) {
   if (d > kMaxDim) return set_error(ZL_ERR_UNSUPPORTED, "prefill: head_dim %d > %d", d, kMaxDim);
   if (num_seqs == 0 || max_seq_len == 0 || H == 0) return ZL_OK;
   if (num_seqs > 65535 || H > 65535)
@@ -269,11 +277,11 @@ zl_status launch_prefill_generic(zl_ctx* ctx, const void* q, const void* k, cons
   if (dtype == ZL_F32)
     prefill_generic_kernel<float><<<grid, kThreads, 0, st>>>(
         (const float*)q, (const float*)k, (const float*)v, cu_seqlens, (float*)out, H, Hkv, d,
-        scale, causal, mod);
+        scale, causal, mod, total_tokens, ctx->d_status);
   else
     prefill_generic_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(
         (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, cu_seqlens,
-        (__nv_bfloat16*)out, H, Hkv, d, scale, causal, mod);
+        (__nv_bfloat16*)out, H, Hkv, d, scale, causal, mod, total_tokens, ctx->d_status);
   ZL_LAUNCH_CHECK(ctx);
   return ZL_OK;
 }

@@ -384,4 +384,14 @@ extern "C" zl_status zl_decode_graph_tokens(zl_decode_graph* g, int64_t* tokens,
   return ZL_OK;
 }
 
+extern "C" zl_status zl_decode_graph_logits(zl_decode_graph* g, float* logits) {
+  if (!g || !logits) return set_error(ZL_ERR_INVALID_ARG, "decode_graph_logits: null");
+  zl_status s = bind_device(g->ctx);
+  if (s != ZL_OK) return s;
+  ZL_CUDA_TRY(cudaEventSynchronize(g->done[g->last]));
+  ZL_CUDA_TRY(cudaMemcpy(logits, g->d_logits, (size_t)g->rows * g->model.vocab * sizeof(float),
+                         cudaMemcpyDeviceToHost));
+  return ZL_OK;
+}
+
 extern "C" int zl_decode_graph_num_kernels(const zl_decode_graph* g) { return g ? g->graph_kernels : 0; }

@@ -62,9 +62,10 @@ zl_status zl_paged_decode(zl_ctx* ctx, const void* q, const void* k_pool, const 
   const float sc = resolve_scale(scale, head_dim);
   cudaStream_t st = S(stream);
   if (dtype == ZL_BF16) {
-    s = launch_decode_bf16_fast(ctx, q, k_pool, v_pool, block_tables, seq_lens, out, num_seqs,
-                                num_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
-                                num_blocks, sc, gqa_map, num_splits, st);
+    s = launch_decode_bf16_fast(ctx, q, k_pool, v_pool, block_tables, seq_lens, nullptr, out,
+                                nullptr, nullptr, nullptr, num_seqs, num_heads, num_kv_heads,
+                                head_dim, block_size, max_blocks_per_seq, num_blocks, sc, gqa_map,
+                                num_splits, st);
     if (s != ZL_ERR_UNSUPPORTED) return s;
   }
   return launch_decode_generic(ctx, q, k_pool, v_pool, block_tables, seq_lens, nullptr, out,
@@ -89,6 +90,13 @@ zl_status zl_paged_decode_partial(zl_ctx* ctx, const void* q, const void* k_pool
   if (num_seqs == 0) return ZL_OK;
   if (!q || !k_pool || !v_pool || !block_tables || !tok_end || !m || !l || !o)
     return set_error(ZL_ERR_INVALID_ARG, "paged_decode_partial: null pointer");
+  if (dtype == ZL_BF16) {
+    s = launch_decode_bf16_fast(ctx, q, k_pool, v_pool, block_tables, tok_end, tok_begin, nullptr,
+                                m, l, o, num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                                max_blocks_per_seq, num_blocks, resolve_scale(scale, head_dim),
+                                gqa_map, 0, S(stream));
+    if (s != ZL_ERR_UNSUPPORTED) return s;
+  }
   return launch_decode_generic(ctx, q, k_pool, v_pool, block_tables, tok_end, tok_begin, nullptr,
                                m, l, o, num_seqs, num_heads, num_kv_heads, head_dim, block_size,
                                max_blocks_per_seq, num_blocks, resolve_scale(scale, head_dim),
@@ -128,7 +136,7 @@ zl_status zl_prefill_varlen(zl_ctx* ctx, const void* q, const void* k, const voi
                           num_kv_heads, head_dim, sc, causal, gqa_map, st);
     if (s != ZL_ERR_UNSUPPORTED) return s;
   }
-  return launch_prefill_generic(ctx, q, k, v, cu_seqlens, num_seqs, max_seq_len, out, num_heads,
+  return launch_prefill_generic(ctx, q, k, v, cu_seqlens, num_seqs, max_seq_len, total_tokens, out, num_heads,
                                 num_kv_heads, head_dim, sc, causal, gqa_map, dtype, st);
 }
 

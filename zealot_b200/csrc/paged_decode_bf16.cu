@@ -51,8 +51,12 @@ struct Partial {
 struct DecodeArgs {
   const __nv_bfloat16* q;      // [B][H][D]
   const int32_t* block_tables; // [B][max_blocks]
-  const int32_t* seq_lens;     // [B]
-  __nv_bfloat16* out;          // [B][H][D]
+  const int32_t* seq_lens;     // [B]; in the partial form the end of each token range
+  const int32_t* tok_begin;    // partial form: first token of each range (null = 0)
+  __nv_bfloat16* out;          // [B][H][D] (normalised form)
+  float* m_out;                // partial form: [B][H] max score (natural-log units)
+  float* l_out;                // partial form: [B][H] sum of e^(s - m)
+  float* o_out;                // partial form: [B][H][D] sum of e^(s - m) v
   Partial* partials;           // [2*W]
   int* counters;               // [0..1] grid barrier words, [2 + b*Hkv + kvh] merge counters;
                                // all zero on entry and exit except the barrier generation
@@ -62,14 +66,32 @@ struct DecodeArgs {
   float scale_log2;            // scale * log2(e)
 };
 
-template <int WARPS, int STAGES>
+template <int WARPS, int STAGES, bool PARTIAL>
 struct Smem {
   static constexpr int kRing = WARPS * STAGES * STAGE;
   static constexpr int kBars = WARPS * STAGES * 8;
   static constexpr int kInfo = WARPS * STAGES * 4;
   static constexpr int kPrefix = (MAX_B + 1) * 4;
-  static constexpr int kTotal = 1024 /*alignment slack*/ + kRing + kBars + kInfo + kPrefix + 16;
+  static constexpr int kJbase = PARTIAL ? MAX_B * 4 : 0;  // table index of each range's first block
+  static constexpr int kTotal = 1024 /*alignment slack*/ + kRing + kBars + kInfo + kPrefix + kJbase + 16;
 };
+static_assert(Smem<4, 6, true>::kTotal <= 232448, "shared memory of the partial form");
+
+// Blocks of sequence b's token range and the block-table index of its first
+// block. The normalised form attends to [0, seq_lens[b]); the partial form to
+// [tok_begin[b], seq_lens[b]). `over` is set when the range runs past the
+// table (the blocks past it are dropped).
+template <bool PARTIAL>
+__device__ __forceinline__ int range_blocks(const DecodeArgs& a, int b, int& jt0, bool& over) {
+  const int e = max(a.seq_lens[b], 0);
+  int s = 0;
+  if (PARTIAL && a.tok_begin) s = max(a.tok_begin[b], 0);
+  jt0 = s / BS;
+  int j1 = (e + BS - 1) / BS;
+  over = j1 > a.max_blocks;
+  if (over) j1 = a.max_blocks;
+  return s < e ? max(j1 - jt0, 0) : 0;
+}
 
 // Swizzled byte offset of (row r, 16-byte chunk c in 0..15) inside a K or V
 // tile: two 2 KB boxes of [16 rows][64 cols], 128-byte swizzle (chunk ^= row%8).
@@ -85,6 +107,45 @@ constexpr int kMaxLastArriver = 16;
 // [gw*TB/W, (gw+1)*TB/W).
 __device__ __forceinline__ int owner_warp(int64_t x, int64_t TB, int64_t W) {
   return (int)(((x + 1) * W - 1) / TB);
+}
+
+// Whether any of the n int32 entries at p is negative; all `nthreads` threads
+// of the CTA call it and share the loads (16-byte loads between a scalar head
+// and tail).
+__device__ __forceinline__ bool any_negative(const int32_t* p, int n, int tid, int nthreads) {
+  const int head = min(n, (int)(((16 - (reinterpret_cast<uintptr_t>(p) & 15)) & 15) >> 2));
+  bool neg = tid < head && __ldg(p + tid) < 0;
+  const int4* p4 = reinterpret_cast<const int4*>(p + head);
+  const int n4 = (n - head) >> 2;
+#pragma unroll 4
+  for (int i = tid; i < n4; i += nthreads) {
+    const int4 v = __ldg(p4 + i);
+    neg |= (v.x | v.y | v.z | v.w) < 0;
+  }
+  const int tail = head + 4 * n4 + tid;
+  if (tail < n) neg |= __ldg(p + tail) < 0;
+  return neg;
+}
+
+// Output of a merged (sequence, head) row: lane L holds elements [4L, 4L+4)
+// of the weighted sum `num` and the row's weight total `den` (relative to the
+// maximum M over the contributors). The normalised form stores num / den in
+// bf16; the partial form stores the triple (M, den, num).
+template <bool PARTIAL>
+__device__ __forceinline__ void emit_merged(const DecodeArgs& a, int64_t row, int lane, float M,
+                                            float den, float4 num) {
+  if constexpr (PARTIAL) {
+    if (lane == 0) { a.m_out[row] = M; a.l_out[row] = den; }
+    reinterpret_cast<float4*>(a.o_out + row * D)[lane] = num;
+  } else {
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(a.out + row * D)[lane] = pk;
+  }
 }
 
 // Grid-wide barrier of a cooperative launch (all CTAs co-resident). words[0]
@@ -123,11 +184,15 @@ __device__ bool grid_barrier(int* words, int* status) {
   return ok_s != 0;
 }
 
-template <int WARPS, int STAGES>
+// PARTIAL = false: normalised bf16 output over [0, seq_lens[b]).
+// PARTIAL = true: the unnormalised triple (m, l, o) of each (sequence, head)
+// over the token range [tok_begin[b], seq_lens[b]), m being the true maximum
+// score (the sequence-split form, merged across GPUs afterwards).
+template <int WARPS, int STAGES, bool PARTIAL>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV) {
-  using SM = Smem<WARPS, STAGES>;
+  using SM = Smem<WARPS, STAGES, PARTIAL>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
@@ -135,6 +200,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + SM::kRing);
   int* info = reinterpret_cast<int*>(base + SM::kRing + SM::kBars);
   int* prefix = reinterpret_cast<int*>(base + SM::kRing + SM::kBars + SM::kInfo);
+  int* jbase = reinterpret_cast<int*>(base + SM::kRing + SM::kBars + SM::kInfo + SM::kPrefix);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -160,12 +226,11 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     for (int k = 0; k < per; k++) {
       const int b = b0 + k;
       if (b < B) {
-        const int len = max(a.seq_lens[b], 0);
-        int nb = (len + BS - 1) / BS;
-        if (nb > a.max_blocks) {
-          if (blockIdx.x == 0) atomicOr(a.status, ZL_DEV_OOB);
-          nb = a.max_blocks;
-        }
+        int jt0;
+        bool over;
+        const int nb = range_blocks<PARTIAL>(a, b, jt0, over);
+        if (over && blockIdx.x == 0) atomicOr(a.status, ZL_DEV_OOB);
+        if (PARTIAL) jbase[b] = jt0;
         local += nb;
         lmax = max(lmax, nb);
       }
@@ -186,8 +251,9 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     for (int k = 0; k < per; k++) {
       const int b = b0 + k;
       if (b < B) {
-        const int len = max(a.seq_lens[b], 0);
-        run += min((len + BS - 1) / BS, a.max_blocks);
+        int jt0;
+        bool over;
+        run += range_blocks<PARTIAL>(a, b, jt0, over);
         prefix[b + 1] = run;
       }
     }
@@ -203,13 +269,24 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   const int64_t W = min((int64_t)gridDim.x * WARPS, TB);
   const int gw = blockIdx.x * WARPS + warp;
 
-  // Sequences with no context produce zeros (CTA 0 writes them).
+  // Sequences with no context produce zeros, (-inf, 0, 0) in the partial
+  // form (CTA 0 writes them).
   if (blockIdx.x == 0) {
     for (int b = warp; b < B; b += WARPS) {
       if (prefix[b + 1] == prefix[b]) {
-        uint2 z = make_uint2(0, 0);
-        for (int i = lane; i < a.H * D / 4; i += 32)
-          reinterpret_cast<uint2*>(a.out + (int64_t)b * a.H * D)[i] = z;
+        if constexpr (PARTIAL) {
+          for (int i = lane; i < a.H; i += 32) {
+            a.m_out[(int64_t)b * a.H + i] = -INFINITY;
+            a.l_out[(int64_t)b * a.H + i] = 0.f;
+          }
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int i = lane; i < a.H * D / 4; i += 32)
+            reinterpret_cast<float4*>(a.o_out + (int64_t)b * a.H * D)[i] = z;
+        } else {
+          uint2 z = make_uint2(0, 0);
+          for (int i = lane; i < a.H * D / 4; i += 32)
+            reinterpret_cast<uint2*>(a.out + (int64_t)b * a.H * D)[i] = z;
+        }
       }
     }
   }
@@ -246,6 +323,29 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     j = (int)(off - (int64_t)kvh * nb);
   };
 
+  // Partial form: a negative table entry before a range's start ends the
+  // sequence before the range, which then holds no tokens. The CTA scans the
+  // entries [0, jbase[b]) of every sequence its warps touch, once, and marks a
+  // sequence so found in the sign bit of jbase[b].
+  if constexpr (PARTIAL) {
+    const int64_t gw0 = (int64_t)blockIdx.x * WARPS;
+    if (gw0 < W) {  // uniform over the CTA
+      const int64_t gw1 = min(gw0 + WARPS, W);
+      int bl, bh, k_, j_;
+      locate(gw0 * TB / W, bl, k_, j_);
+      locate(gw1 * TB / W - 1, bh, k_, j_);
+      for (int b = bl; b <= bh; b++) {
+        const int n = jbase[b];
+        bool neg = false;
+        if (n > 0) neg = any_negative(a.block_tables + (int64_t)b * a.max_blocks, n, tid, WARPS * 32);
+        if (__syncthreads_or(neg) && tid == 0) jbase[b] = n | (int)0x80000000;
+      }
+    }
+    __syncthreads();
+  }
+  auto table_base = [&](int b) -> int { return PARTIAL ? (jbase[b] & 0x7fffffff) : 0; };
+  auto cut_before = [&](int b) -> bool { return PARTIAL && jbase[b] < 0; };
+
   if (nwork > 0) {
   const uint32_t ring = base_u32 + warp * STAGES * STAGE;
   uint64_t* wbars = bars + warp * STAGES;
@@ -265,11 +365,13 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   {
     int b, kvh, j;
     locate(f0, b, kvh, j);
-    bool neg = false;
+    const int t_lo = table_base(b);  // entries before the range: cut_before(b)
+    j += t_lo;
+    bool neg = cut_before(b);
     const int32_t* tb = tables + (int64_t)b * a.max_blocks;
     // eight independent loads per lane in flight: one memory latency for the
     // first 256 entries instead of one per 32
-    for (int t0 = 0; t0 < j; t0 += 256) {
+    for (int t0 = t_lo; t0 < j; t0 += 256) {
       int v[8];
 #pragma unroll
       for (int u = 0; u < 8; u++) {
@@ -285,12 +387,14 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   auto build_chunk = [&](int base) {
     const int idx = base + lane;
     const bool ok = idx < nwork;
-    int seg = -1, e = 0, b = 0, kvh = 0, j = 0, len = 0;
+    int seg = -1, e = 0, b = 0, kvh = 0, j = 0, len = 0, beg = 0;
     if (ok) {
       locate(f0 + idx, b, kvh, j);
       seg = b * Hkv + kvh;
+      j += table_base(b);  // j: table index from here on
       e = tables[(int64_t)b * a.max_blocks + j];
       len = a.seq_lens[b];  // issued with the table read: one latency, not two
+      if constexpr (PARTIAL) beg = a.tok_begin ? a.tok_begin[b] : 0;
     }
     const unsigned negm = __ballot_sync(0xffffffffu, ok && e < 0);
     const int prev = __shfl_up_sync(0xffffffffu, seg, 1);
@@ -299,13 +403,16 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     const int my_start = 31 - __clz(startm & upto);
     bool trunc = (negm & upto & ~((1u << my_start) - 1u)) != 0;
     if (my_start == 0 && seg == carry_seg && carry_trunc) trunc = true;
+    if (ok && cut_before(b)) trunc = true;
     int nv = 0, y = 0;
     if (ok && !trunc) {
       if ((int64_t)e >= a.num_blocks) {
         atomicOr(a.status, ZL_DEV_OOB);
       } else {
-        const int nb = prefix[b + 1] - prefix[b];
-        nv = (j == nb - 1) ? (len - j * BS) : BS;
+        // valid tokens [lo, hi) of the block; nv packs hi | lo << 8
+        const int hi = min(len - j * BS, BS);
+        const int lo = PARTIAL ? max(beg - j * BS, 0) : 0;
+        nv = hi | (lo << 8);
         y = (int)(((int64_t)e * Hkv + kvh) * BS);
       }
     }
@@ -413,6 +520,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       }
     }
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float tm0 = -INFINITY, tm1 = -INFINITY;  // true maxima (partial form)
     float o[8][4];
 #pragma unroll
     for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
@@ -428,21 +536,24 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         timed_out = true;
         break;
       }
-      int slotB = slotA, nvB = 0;
-      const int nvA = winfo[slotA];
+      int slotB = slotA, nvB = 0, loB = 0;
+      const int infoA = winfo[slotA];
+      const int nvA = infoA & 0xff, loA = PARTIAL ? (infoA >> 8) : 0;
       if (two) {
         slotB = (i + 1) % STAGES;
         if (!mbar_wait_warp(smem_u32(&wbars[slotB]), (uint32_t)(((i + 1) / STAGES) & 1), a.status)) {
           timed_out = true;
           break;
         }
-        nvB = winfo[slotB];
+        const int infoB = winfo[slotB];
+        nvB = infoB & 0xff;
+        if constexpr (PARTIAL) loB = infoB >> 8;
       }
       if (nvA > 0 || nvB > 0) {
         uint32_t kA = ring + slotA * STAGE, kB = ring + slotB * STAGE;
         if (nvA == 0) kA = kB;
         if (nvB == 0) kB = kA;
-        // zero V rows past the context so 0 * garbage cannot be NaN
+        // zero V rows outside the valid tokens so 0 * garbage cannot be NaN
         if (nvA > 0 && nvA < BS) {
           uint8_t* vt = base + (kA + TILE - base_u32);
           for (int x = lane; x < (BS - nvA) * 16; x += 32) {
@@ -455,6 +566,18 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
           for (int x = lane; x < (BS - nvB) * 16; x += 32) {
             const int r = nvB + (x >> 4), c = x & 15;
             *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        if constexpr (PARTIAL) {  // rows before the range start
+          if (nvA > 0 && loA > 0) {
+            uint8_t* vt = base + (kA + TILE - base_u32);
+            for (int x = lane; x < loA * 16; x += 32)
+              *reinterpret_cast<uint4*>(vt + tile_off(x >> 4, x & 15)) = make_uint4(0, 0, 0, 0);
+          }
+          if (nvB > 0 && loB > 0) {
+            uint8_t* vt = base + (kB + TILE - base_u32);
+            for (int x = lane; x < loB * 16; x += 32)
+              *reinterpret_cast<uint4*>(vt + tile_off(x >> 4, x & 15)) = make_uint4(0, 0, 0, 0);
           }
         }
         __syncwarp();
@@ -475,8 +598,8 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         }
         // mask + scale to log2 units
         const float sc = a.scale_log2;
-        const bool va0 = quad < nvA, va1 = quad + 8 < nvA;
-        const bool vb0 = quad < nvB, vb1 = quad + 8 < nvB;
+        const bool va0 = quad < nvA && quad >= loA, va1 = quad + 8 < nvA && quad + 8 >= loA;
+        const bool vb0 = quad < nvB && quad >= loB, vb1 = quad + 8 < nvB && quad + 8 >= loB;
         sA[0] = va0 ? (sA[0] + sA2[0]) * sc : -INFINITY;
         sA[1] = va0 ? (sA[1] + sA2[1]) * sc : -INFINITY;
         sA[2] = va1 ? (sA[2] + sA2[2]) * sc : -INFINITY;
@@ -487,6 +610,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         sB[3] = vb1 ? (sB[3] + sB2[3]) * sc : -INFINITY;
         const float c0m = fmaxf(fmaxf(sA[0], sA[2]), fmaxf(sB[0], sB[2]));
         const float c1m = fmaxf(fmaxf(sA[1], sA[3]), fmaxf(sB[1], sB[3]));
+        if constexpr (PARTIAL) { tm0 = fmaxf(tm0, c0m); tm1 = fmaxf(tm1, c1m); }
         const bool grow = c0m > m0 + kLazy || c1m > m1 + kLazy;
         if (__any_sync(0xffffffffu, grow)) {
           float bm0 = c0m, bm1 = c1m;
@@ -548,8 +672,37 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       L1 += __shfl_xor_sync(0xffffffffu, L1, off);
     }
     const int n0 = 2 * qid, n1 = 2 * qid + 1;  // head columns of this lane
+    float mo0 = m0 * LN2, mo1 = m1 * LN2;      // reference maxima, natural-log units
+    if constexpr (PARTIAL) {
+      // Re-base (l, o) from the lazily moved running max to the true maximum
+      // of the range, so that m is the maximum score as the triple promises.
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, off));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, off));
+      }
+      const float f0 = tm0 == -INFINITY ? 0.f : ex2(m0 - tm0);
+      const float f1 = tm1 == -INFINITY ? 0.f : ex2(m1 - tm1);
+      L0 *= f0; L1 *= f1;
+#pragma unroll
+      for (int t = 0; t < 8; t++) { o[t][0] *= f0; o[t][2] *= f0; o[t][1] *= f1; o[t][3] *= f1; }
+      mo0 = tm0 * LN2; mo1 = tm1 * LN2;
+    }
     const bool whole = (seg_S >= f0) && (seg_E <= f1);
-    if (whole) {
+    if (whole && PARTIAL) {
+      const int64_t row = (int64_t)cb * a.H + head0;
+      if (quad == 0) {
+        if (n0 < G) { a.m_out[row + n0] = mo0; a.l_out[row + n0] = L0; }
+        if (n1 < G) { a.m_out[row + n1] = mo1; a.l_out[row + n1] = L1; }
+      }
+      float* ob = a.o_out + row * D;
+#pragma unroll
+      for (int t = 0; t < 8; t++) {
+        const int d0 = 16 * t + quad;
+        if (n0 < G) { ob[n0 * D + d0] = o[t][0]; ob[n0 * D + d0 + 8] = o[t][2]; }
+        if (n1 < G) { ob[n1 * D + d0] = o[t][1]; ob[n1 * D + d0 + 8] = o[t][3]; }
+      }
+    } else if (whole) {
       const float i0 = L0 > 0.f ? 1.f / L0 : 0.f, i1 = L1 > 0.f ? 1.f / L1 : 0.f;
       __nv_bfloat16* ob = a.out + ((int64_t)cb * a.H + head0) * D;
 #pragma unroll
@@ -568,8 +721,8 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       const int e = (seg_S <= f0 && f0 < seg_E) ? 0 : 1;
       Partial* pp = a.partials + 2 * gw + e;
       if (quad == 0) {
-        if (n0 < G) { pp->m[n0] = m0 * LN2; pp->l[n0] = L0; }
-        if (n1 < G) { pp->m[n1] = m1 * LN2; pp->l[n1] = L1; }
+        if (n0 < G) { pp->m[n0] = mo0; pp->l[n0] = L0; }
+        if (n1 < G) { pp->m[n1] = mo1; pp->l[n1] = L1; }
       }
 #pragma unroll
       for (int t = 0; t < 8; t++) {
@@ -683,15 +836,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         for (int n = 0; n < MAX_G; n++) {
 #pragma unroll
           for (int off = 16; off; off >>= 1) den[n] += __shfl_xor_sync(0xffffffffu, den[n], off);
-          if (n < G) {
-            const float inv = den[n] > 0.f ? 1.f / den[n] : 0.f;
-            __nv_bfloat162 lo = __floats2bfloat162_rn(num[n].x * inv, num[n].y * inv);
-            __nv_bfloat162 hi = __floats2bfloat162_rn(num[n].z * inv, num[n].w * inv);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t*>(&lo);
-            pk.y = *reinterpret_cast<uint32_t*>(&hi);
-            reinterpret_cast<uint2*>(a.out + ((int64_t)cb * a.H + head0 + n) * D)[lane] = pk;
-          }
+          if (n < G) emit_merged<PARTIAL>(a, (int64_t)cb * a.H + head0 + n, lane, M[n], den[n], num[n]);
         }
         if (lane == 0) a.counters[cidx] = 0;
       }
@@ -768,13 +913,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       }
 #pragma unroll
       for (int off = 16; off; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
-      __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&lo);
-      pk.y = *reinterpret_cast<uint32_t*>(&hi);
-      reinterpret_cast<uint2*>(a.out + ((int64_t)b * a.H + kvh * G + n) * D)[lane] = pk;
+      emit_merged<PARTIAL>(a, (int64_t)b * a.H + kvh * G + n, lane, M, den, num);
     }
   }
 }
@@ -849,18 +988,20 @@ zl_status make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t cols, uint6
 }
 
 zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool, const void* v_pool,
-                                  const int32_t* block_tables, const int32_t* seq_lens, void* out,
-                                  int B, int H, int Hkv, int d, int bs, int max_blocks,
+                                  const int32_t* block_tables, const int32_t* seq_lens,
+                                  const int32_t* tok_begin, void* out, float* m_out, float* l_out,
+                                  float* o_out, int B, int H, int Hkv, int d, int bs, int max_blocks,
                                   int64_t num_blocks, float scale, zl_gqa_map map, int num_splits,
                                   cudaStream_t st) {
   (void)num_splits;
+  const bool partial = o_out != nullptr;
   if (d != D || bs != BS || Hkv <= 0 || H % Hkv != 0 || H / Hkv > MAX_G || B > MAX_B ||
       map != ZL_GQA_GROUPED && H != Hkv)
     return ZL_ERR_UNSUPPORTED;
   const uint64_t rows = (uint64_t)num_blocks * Hkv * BS;
   if (rows == 0 || rows >= (1ull << 31)) return ZL_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
-       reinterpret_cast<uintptr_t>(out)) & 15)
+       reinterpret_cast<uintptr_t>(partial ? (void*)o_out : out)) & 15)
     return ZL_ERR_UNSUPPORTED;
   if (B == 0) return ZL_OK;
 
@@ -881,7 +1022,11 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
   args.q = (const __nv_bfloat16*)q;
   args.block_tables = block_tables;
   args.seq_lens = seq_lens;
+  args.tok_begin = tok_begin;
   args.out = (__nv_bfloat16*)out;
+  args.m_out = m_out;
+  args.l_out = l_out;
+  args.o_out = o_out;
   args.partials = (Partial*)ctx->workspace;
   args.counters = (int*)ctx->counters;
   args.status = ctx->d_status;
@@ -889,15 +1034,28 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
   args.num_blocks = num_blocks;
   args.scale_log2 = scale * LOG2E;
 
-  using SM = Smem<kWarps, kStages>;
-  auto kern = paged_decode_bf16_kernel<kWarps, kStages>;
-  // the shared-memory limit is a per-device attribute of the function
-  static std::atomic<uint64_t> attr_set{0};
-  if (ctx->device < 64 && !(attr_set.load() & (1ull << ctx->device))) {
-    ZL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal));
-    attr_set.fetch_or(1ull << ctx->device);
+  // the shared-memory limit is a per-device attribute of each function
+  auto set_smem = [&](auto kern, int bytes, std::atomic<uint64_t>& done) -> cudaError_t {
+    if (ctx->device < 64 && !(done.load() & (1ull << ctx->device))) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e != cudaSuccess) return e;
+      done.fetch_or(1ull << ctx->device);
+    }
+    return cudaSuccess;
+  };
+  if (partial) {
+    using SM = Smem<kWarps, kStages, true>;
+    auto kern = paged_decode_bf16_kernel<kWarps, kStages, true>;
+    static std::atomic<uint64_t> attr_set{0};
+    ZL_CUDA_TRY(set_smem(kern, SM::kTotal, attr_set));
+    ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
+  } else {
+    using SM = Smem<kWarps, kStages, false>;
+    auto kern = paged_decode_bf16_kernel<kWarps, kStages, false>;
+    static std::atomic<uint64_t> attr_set{0};
+    ZL_CUDA_TRY(set_smem(kern, SM::kTotal, attr_set));
+    ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
   }
-  ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
   ZL_LAUNCH_CHECK(ctx);
   return ZL_OK;
 }
@@ -924,43 +1082,47 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
 // different streams, or from different host threads without ordering) race
 // on it and give wrong results. Calls ordered on one stream are safe; each
 // call clears the merge counters it uses before its kernel runs.
+// Device-side errors go to the caller's status word, which is required: the
+// call itself returns ZL_OK once the kernel is queued.
 namespace {
 
 constexpr int kNoAllocMaxCtas = 160;            // >= 148 SMs of a B200
 constexpr int kNoAllocMaxSegments = 16384;      // (sequence, kv head) pairs per call
 struct NoAllocScratch {
   Partial partials[2 * kNoAllocMaxCtas * kWarps];
-  int status;                          // device flags when the caller passes no status word
-  int counters[2 + kNoAllocMaxSegments];  // must directly follow `status` (cleared together)
+  int counters[2 + kNoAllocMaxSegments];  // grid-barrier words, then one per (sequence, kv head)
 };
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
 constexpr int kMaxDevices = 64;
 struct NoAllocDevice {
-  NoAllocScratch* scratch = nullptr;  // device address of g_noalloc_scratch
+  NoAllocScratch* scratch = nullptr;  // device address of g_noalloc_scratch when last resolved
   int num_sms = 0;
 };
 NoAllocDevice g_noalloc_dev[kMaxDevices];
 std::mutex g_noalloc_mu;
 
-// Once per device, with that device current: resolve the array's device
-// address (the host-side symbol is only a stand-in and must never be handed
-// to a kernel) and raise the kernel's dynamic shared-memory limit.
+// Every call, with the device current: resolve the array's device address
+// (the host-side symbol is only a stand-in and must never be handed to a
+// kernel; the lookup is cheap and allocates nothing). When the address is new
+// -- the first call on the device, or the module was loaded again after a
+// device reset -- also read the SM count and raise the kernel's dynamic
+// shared-memory limit, which a reset drops as well.
 zl_status noalloc_setup(int dev, NoAllocDevice** out) {
   std::lock_guard<std::mutex> g(g_noalloc_mu);
   NoAllocDevice& nd = g_noalloc_dev[dev];
-  if (!nd.scratch) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess)
-      return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: cudaGetSymbolAddress failed: %s",
-                           cudaGetErrorString(e));
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess)
+    return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                         cudaGetErrorString(e));
+  if (nd.scratch != p) {
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess)
       return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: SM count: %s", cudaGetErrorString(e));
-    using SM = Smem<kWarps, kStages>;
-    e = cudaFuncSetAttribute(paged_decode_bf16_kernel<kWarps, kStages>,
+    using SM = Smem<kWarps, kStages, false>;
+    e = cudaFuncSetAttribute(paged_decode_bf16_kernel<kWarps, kStages, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal);
     if (e != cudaSuccess)
       return zl::set_error(ZL_ERR_CUDA, "paged_decode_noalloc: shared-memory limit: %s",
@@ -998,6 +1160,10 @@ extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, 
   if (rows >= (1ull << 31))
     return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: pool of %lld blocks is too large",
                      (long long)num_blocks);
+  if (!status)
+    return set_error(ZL_ERR_INVALID_ARG,
+                     "paged_decode_noalloc: a device status word is required (device-side errors "
+                     "are reported only there)");
   if (num_seqs == 0) return ZL_OK;
   if (!q || !k_pool || !v_pool || !block_tables || !seq_lens || !out || rows == 0)
     return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: null pointer or empty pool");
@@ -1018,28 +1184,29 @@ extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, 
 
   cudaStream_t st = S(stream);
   NoAllocScratch* scr = nd->scratch;
-  // The merge counters and grid-barrier words (and the fallback status word in
-  // front of them) must start at zero; clearing them per call also recovers
+  // The grid-barrier words and the merge counters of this call's (sequence,
+  // kv head) pairs must start at zero; clearing them per call also recovers
   // from a call whose kernel gave up part-way.
-  e = cudaMemsetAsync(&scr->status, 0, sizeof(int) * (3 + (size_t)num_seqs * num_kv_heads), st);
+  e = cudaMemsetAsync(scr->counters, 0, sizeof(int) * (2 + (size_t)num_seqs * num_kv_heads), st);
   if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: counter clear: %s", cudaGetErrorString(e));
 
   DecodeArgs args;
   args.q = (const __nv_bfloat16*)q;
   args.block_tables = block_tables;
   args.seq_lens = seq_lens;
+  args.tok_begin = nullptr;
   args.out = (__nv_bfloat16*)out;
+  args.m_out = args.l_out = args.o_out = nullptr;
   args.partials = scr->partials;
   args.counters = scr->counters;
-  // Without a caller status word, device-side flags land in the scratch one.
-  args.status = status ? status : &scr->status;
+  args.status = status;
   args.B = num_seqs; args.H = num_heads; args.Hkv = num_kv_heads; args.G = num_heads / num_kv_heads;
   args.max_blocks = max_blocks_per_seq;
   args.num_blocks = num_blocks;
   args.scale_log2 = resolve_scale(scale, D) * LOG2E;
   const int grid = nd->num_sms < kNoAllocMaxCtas ? nd->num_sms : kNoAllocMaxCtas;
-  using SM = Smem<kWarps, kStages>;
-  e = launch_cooperative(paged_decode_bf16_kernel<kWarps, kStages>, grid, SM::kTotal, st, args, tk, tv);
+  using SM = Smem<kWarps, kStages, false>;
+  e = launch_cooperative(paged_decode_bf16_kernel<kWarps, kStages, false>, grid, SM::kTotal, st, args, tk, tv);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: launch: %s", cudaGetErrorString(e));
   return ZL_OK;

@@ -57,6 +57,7 @@ struct PrefillArgs {
   const int32_t* cu_seqlens;
   __nv_bfloat16* out;  // [T][H][D]
   int* status;
+  int64_t total_tokens;  // rows of q / k / v / out: every sequence must end at or before it
   int H, Hkv, G, num_seqs;
   float scale_log2;
   int causal;
@@ -99,7 +100,17 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
   const int hp = blockIdx.x - s * hp_count;
   const int t = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles launch first
   const int start = a.cu_seqlens[s];
-  const int L = a.cu_seqlens[s + 1] - start;
+  const int end = a.cu_seqlens[s + 1];
+  // cu_seqlens comes from device memory: a sequence outside [0, total_tokens]
+  // or running backwards is reported and skipped, so no load or store leaves
+  // the caller's buffers. A sequence longer than the launch's max_seq_len
+  // (rows no tile covers) is reported and skipped too. Uniform over the CTA.
+  if (start < 0 || end < start || (int64_t)end > a.total_tokens ||
+      (int64_t)(end - start) > (int64_t)BM * gridDim.y) {
+    if (threadIdx.x == 0 && blockIdx.y == 0) atomicOr(a.status, ZL_DEV_OOB);
+    return;
+  }
+  const int L = end - start;
   if (BM * t >= L) return;  // uniform: this tile is past the sequence
   if (aborted(a.status)) return;  // an earlier CTA timed out: do not queue behind it
   const int h0 = hp * NQ;
@@ -381,6 +392,7 @@ zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const voi
   args.cu_seqlens = cu_seqlens;
   args.out = (__nv_bfloat16*)out;
   args.status = ctx->d_status;
+  args.total_tokens = total_tokens;
   args.H = H; args.Hkv = Hkv; args.G = H / Hkv; args.num_seqs = num_seqs;
   args.scale_log2 = scale * LOG2E;
   args.causal = causal ? 1 : 0;

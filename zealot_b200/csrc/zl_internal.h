@@ -30,8 +30,14 @@ struct zl_ctx {
   // NCCL (loaded at run time)
   void* nccl_comm = nullptr;
   int nranks = 1, rank = 0;
-  void* gather_buf = nullptr;
+  void* gather_buf = nullptr;     // sized once at zl_nccl_init: nranks x max_rows x (2 + max_d) fp32
   size_t gather_bytes = 0;
+  int64_t nccl_max_rows = 0;
+  int nccl_max_d = 0;
+  int nccl_timeout_ms = 0;        // bound of zl_nccl_wait / zl_check_status on a pending collective
+  cudaEvent_t nccl_done = nullptr;  // recorded after the last enqueued all-gather
+  bool nccl_pending = false;      // an all-gather was enqueued and not yet seen complete
+  bool nccl_aborted = false;      // the communicator was aborted (a peer was lost)
   // decoder-step activations (residual stream, q/k/v, attention out, MLP)
   void* activations = nullptr;
   size_t activation_bytes = 0;
@@ -83,15 +89,20 @@ zl_status launch_decode_generic(zl_ctx* ctx, const void* q, const void* k_pool,
                                 int B, int H, int Hkv, int d, int bs, int max_blocks,
                                 int64_t num_blocks, float scale, zl_gqa_map map,
                                 zl_dtype dtype, cudaStream_t st);
+// Both prefill launchers check cu_seqlens on the device against total_tokens
+// (ZL_DEV_OOB and the sequence skipped when it leaves [0, total_tokens]).
 zl_status launch_prefill_generic(zl_ctx* ctx, const void* q, const void* k, const void* v,
                                  const int32_t* cu_seqlens, int num_seqs, int max_seq_len,
-                                 void* out, int H, int Hkv, int d, float scale, int causal,
-                                 zl_gqa_map map, zl_dtype dtype, cudaStream_t st);
+                                 int64_t total_tokens, void* out, int H, int Hkv, int d, float scale,
+                                 int causal, zl_gqa_map map, zl_dtype dtype, cudaStream_t st);
 // Fast bf16 decode (paged_decode_bf16.cu). Returns ZL_ERR_UNSUPPORTED when the
 // shape is outside its envelope so the caller can use the CUDA-core kernel.
+// With o_out != nullptr it computes the partial triple (m_out, l_out, o_out)
+// over [tok_begin[b], seq_lens[b]) instead of the normalised `out`.
 zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool,
                                   const void* v_pool, const int32_t* block_tables,
-                                  const int32_t* seq_lens, void* out, int B, int H, int Hkv,
+                                  const int32_t* seq_lens, const int32_t* tok_begin, void* out,
+                                  float* m_out, float* l_out, float* o_out, int B, int H, int Hkv,
                                   int d, int bs, int max_blocks, int64_t num_blocks, float scale,
                                   zl_gqa_map map, int num_splits, cudaStream_t st);
 zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const void* v,
@@ -107,6 +118,11 @@ zl_status launch_matmul_f32(zl_ctx* ctx, const float* a, const float* b, float* 
                             int64_t k, int64_t n, cudaStream_t st);
 zl_status launch_gather_rows_f32(zl_ctx* ctx, const float* src, const int32_t* rows, int64_t n,
                                  int64_t width, float* dst, cudaStream_t st);
+
+// Waits (bounded by the context's NCCL timeout) for the last enqueued NCCL
+// all-gather; aborts the communicator when it does not finish in time or NCCL
+// reports an asynchronous error. ZL_OK when nothing is pending.
+zl_status nccl_wait_pending(zl_ctx* ctx, int timeout_ms);
 
 // Default softmax scale 1/sqrt(d) computed like src/attention/mod.rs:53.
 inline float resolve_scale(float scale, int d) {

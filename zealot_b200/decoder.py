@@ -258,6 +258,13 @@ class DecodeGraph:
             self._lp.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
         return self._tok.copy(), self._lp.copy()
 
+    def logits(self):
+        """Waits for the last step; the logits it sampled from, float32 [rows][vocab]."""
+        out = np.empty((self.rows, self.dec.cfg.vocab), np.float32)
+        check(self.ctx.lib.zl_decode_graph_logits(self.handle,
+                                                  out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        return out
+
     @property
     def num_kernels(self) -> int:
         return int(self.ctx.lib.zl_decode_graph_num_kernels(self.handle))

@@ -125,11 +125,16 @@ class SequenceSplitDecoder:
     """Decode for sequences whose KV is split across GPUs: local partial triples,
     NCCL all-gather over NVLink, merge kernel. One instance per process/GPU."""
 
-    def __init__(self, ctx: GpuContext, rank: int, world: int, broadcast_id, watch: PeerWatch | None = None):
+    def __init__(self, ctx: GpuContext, rank: int, world: int, broadcast_id, watch: PeerWatch | None = None,
+                 max_rows: int = 4096, max_head_dim: int = 128, timeout_ms: int = 10000):
         """`broadcast_id(bytes_or_None) -> bytes` shares rank 0's 128-byte NCCL id
         (e.g. via torch.distributed.broadcast_object_list). With `watch`, every
         decode() first checks that all ranks reached the same step (PeerLost
-        otherwise) before it launches the partial decode and the NCCL merge."""
+        otherwise) before it launches the partial decode and the NCCL merge.
+        The gather buffer is sized once for steps of up to `max_rows` (sequence,
+        head) rows; `timeout_ms` bounds every wait on a collective, after which
+        the communicator is aborted (DeviceTimeout) instead of waiting for a
+        peer that is gone."""
         self.ctx, self.lib, self.rank, self.world = ctx, ctx.lib, rank, world
         self.watch, self._step = watch, 0
         buf = (ctypes.c_uint8 * 128)()
@@ -139,7 +144,7 @@ class SequenceSplitDecoder:
         else:
             uid = broadcast_id(None)
         ctypes.memmove(buf, uid, 128)
-        check(self.lib.zl_nccl_init(ctx.handle, buf, world, rank))
+        check(self.lib.zl_nccl_init(ctx.handle, buf, world, rank, max_rows, max_head_dim, timeout_ms))
 
     def decode(self, q, k_pool, v_pool, block_tables, tok_begin, tok_end, out, num_heads: int,
                num_kv_heads: int, head_dim: int, block_size: int, max_blocks_per_seq: int,
@@ -162,6 +167,15 @@ class SequenceSplitDecoder:
             max_blocks_per_seq, num_blocks, scale, gqa_map, dtype_code(q.dtype), st))
         check(self.lib.zl_nccl_merge(self.ctx.handle, ptr(m), ptr(l), ptr(o), B * num_heads,
                                      head_dim, ptr(out), dtype_code(out.dtype), st))
+
+    def wait(self, timeout_ms: int = 0) -> None:
+        """Bounded wait for the last step's all-gather (0: the init timeout). Raises
+        DeviceTimeout (and aborts the communicator) when a peer never joined it."""
+        check(self.lib.zl_nccl_wait(self.ctx.handle, timeout_ms))
+
+    def abort(self) -> None:
+        """Aborts the communicator (e.g. after PeerLost); later decode() calls fail."""
+        check(self.lib.zl_nccl_abort(self.ctx.handle))
 
     def close(self) -> None:
         check(self.lib.zl_nccl_finalize(self.ctx.handle))
