@@ -3,22 +3,33 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Headline workload: one paged-decode attention step of a
-Llama-3-8B layer -- 64 sequences per GPU, 32 query / 8 kv heads, head_dim 128,
-bf16, context U[512, 4096], block_size 16, block tables drawn from a seeded
-random permutation of a 65536-block pool, q/K/V ~ N(0, 1). A step is one
+Llama-3-8B layer -- 64 sequences, 32 query / 8 kv heads, head_dim 128, bf16,
+context U[512, 4096], block_size 16, block tables drawn from a seeded random
+permutation of a 65536-block pool, q/K/V ~ N(0, 1). A step is one
 zl_paged_decode launch over every sequence; tokens/s = sequences / step time.
 
-Multi-GPU (torchrun, one process per GPU): kv-head-group sharding, weak
-scaling -- at N GPUs the job is 64*N sequences and rank r owns kv heads
-[r*8/N, (r+1)*8/N) (and their query heads) of all of them, so every rank moves
-the same bytes as the 1-GPU step and no collective touches the data path.
+Multi-GPU (torchrun, one process per GPU): the same fixed job, kv-head-group
+sharded (strong scaling): rank r owns kv heads [r*8/N, (r+1)*8/N) of all 64
+sequences and their query heads; no collective touches the data path. The step
+time is the maximum over ranks of CUDA-event time. At N >= 2 a rank's KV per
+step is at most 290 MB, so consecutive steps rotate over four sets of block
+tables on disjoint pool blocks (same context lengths): no step finds the
+previous steps' KV in the 126 MB L2.
 
-The JSON line carries value (device-resident inputs), e2e (through the C ABI
-with pinned host buffers copied in and out inside the timed region), the
-roofline of the decode kernel, side measurements of the C3 prefill and
-reshape_and_cache, sampled clocks, and the CPU baseline (the oracle, a C
-restatement of the reference CPU attention). `--impl reference` times that
-oracle alone, multi-threaded on the host cores.
+The JSON line also carries, at every N (per-rank times and roofline fractions
+in each):
+  c5                 BASELINE config 5 (8 x 131072 tokens, 64 / 8 heads), its kv
+                     heads sharded over the ranks, split-KV inside each GPU;
+  seq_split          (N >= 2) the same C5 data split by token range instead:
+                     each rank's partial triples (zl_paged_decode_partial) are
+                     all-gathered over NVLink and merged (zl_nccl_merge); the
+                     merged output is compared with the head-sharded one;
+  prefill            C3 varlen causal prefill, heads sharded like the decode;
+  reshape_and_cache  the C3 tokens scattered into a paged pool, heads sharded;
+plus e2e (the headline through the C ABI with pinned host buffers copied in and
+out inside the timed region), sampled clocks and, at N = 1, CPU baselines (the
+oracle, a C restatement of the reference CPU path, on one thread, as the
+reference runs). `--impl reference` times that oracle alone on all host cores.
 """
 from __future__ import annotations
 
@@ -35,19 +46,20 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-B_PER_GPU, H, HKV, D, BS, NUM_BLOCKS, MAX_BLOCKS = 64, 32, 8, 128, 16, 65536, 256
+B_C2, H, HKV, D, BS, NUM_BLOCKS, MAX_BLOCKS = 64, 32, 8, 128, 16, 65536, 256
+B_PER_GPU = B_C2  # the 1-GPU job (kept for the CPU tests of the byte model)
 CTX_LO, CTX_HI = 512, 4096
 SEED = 2024
+ROTATE = 4              # block-table sets rotated at N >= 2
+L2_FLUSH_BYTES = 256 << 20
 
-# Decode workloads. C2 (headline): Llama-3-8B layer, 64 sequences per GPU, weak
-# scaling over kv-head groups. C5: Llama-3-70B attention, 8 sequences of
-# 131072 tokens, the fixed job's kv-head groups sharded over the GPUs (strong).
+# Decode workloads. C2 (headline): Llama-3-8B layer, the fixed 64-sequence job.
+# C5: Llama-3-70B attention, the fixed 8 x 131072 job. Both kv-head sharded.
 DECODE_SHAPES = {
-    "decode": dict(name="C2", b_per_gpu=64, b_total=None, H=32, HKV=8, ctx=(512, 4096), max_blocks=256,
-                   scaling="weak"),
-    "c5": dict(name="C5", b_per_gpu=None, b_total=8, H=64, HKV=8, ctx=(131072, 131072), max_blocks=8192,
-               scaling="strong"),
+    "decode": dict(name="C2", B=64, H=32, HKV=8, ctx=(512, 4096), max_blocks=256, seed=SEED),
+    "c5": dict(name="C5", B=8, H=64, HKV=8, ctx=(131072, 131072), max_blocks=8192, seed=SEED + 5),
 }
+C3 = dict(seqs=16, lo=256, hi=8192, seed=3)
 
 
 def log(*a):
@@ -56,22 +68,23 @@ def log(*a):
 
 # ------------------------------------------------------------------ workload
 
-def make_lens_tables(world: int, pool_blocks: int = NUM_BLOCKS, shape=None):
-    """Context lengths and block tables of the global batch (identical on every rank)."""
+def make_lens_tables(shape=None, n_sets: int = 1, pool_blocks: int = NUM_BLOCKS):
+    """Context lengths and `n_sets` block tables [n_sets][B][max_blocks] over disjoint
+    blocks of one seeded permutation of the pool (identical on every rank)."""
     shape = shape or DECODE_SHAPES["decode"]
-    rng = np.random.default_rng(SEED)
-    B = shape["b_total"] or shape["b_per_gpu"] * world
+    rng = np.random.default_rng(shape["seed"])
+    B = shape["B"]
     lo, hi = shape["ctx"]
     lens = rng.integers(lo, hi + 1, size=B).astype(np.int32)
     nblk = (lens + BS - 1) // BS
-    # per rank the pool holds its own kv heads' blocks; the tables index it
-    pool_blocks = max(pool_blocks, int(nblk.sum()))
+    pool_blocks = max(pool_blocks, int(nblk.sum()) * n_sets)
     perm = rng.permutation(pool_blocks).astype(np.int32)
-    tables = np.full((B, shape["max_blocks"]), -1, np.int32)
+    tables = np.full((n_sets, B, shape["max_blocks"]), -1, np.int32)
     off = 0
-    for b in range(B):
-        tables[b, : nblk[b]] = perm[off: off + nblk[b]]
-        off += nblk[b]
+    for s in range(n_sets):
+        for b in range(B):
+            tables[s, b, : nblk[b]] = perm[off: off + nblk[b]]
+            off += nblk[b]
     return lens, tables, pool_blocks
 
 
@@ -82,6 +95,15 @@ def algorithmic_bytes(lens, hkv, h, esize=2):
     kv = int(lens.astype(np.int64).sum()) * hkv * D * 2 * esize
     qo = len(lens) * h * D * 2 * esize
     return kv + qo + int(nblk.sum()) * 4 + len(lens) * 4
+
+
+def c3_lens():
+    rng = np.random.default_rng(C3["seed"])
+    return rng.integers(C3["lo"], C3["hi"] + 1, size=C3["seqs"]), rng
+
+
+def prefill_flop(lens, heads):
+    return sum(4 * heads * D * int(L) * (int(L) + 1) / 2 for L in lens)
 
 
 # -------------------------------------------------------------------- clocks
@@ -135,6 +157,75 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+
+
+# -------------------------------------------------------------- multi-rank
+
+class Ranks:
+    """Barrier, max over ranks and per-rank gathers (no-ops on one process)."""
+
+    def __init__(self, dist, rank, world):
+        self.dist, self.rank, self.world = dist, rank, world
+
+    def barrier(self):
+        import torch
+        if self.dist is not None:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+
+    def gather(self, x: float) -> list:
+        import torch
+        if self.dist is None:
+            return [x]
+        t = torch.zeros(self.world, device="cuda", dtype=torch.float64)
+        t[self.rank] = x
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return [float(v) for v in t.cpu()]
+
+    def max(self, x: float) -> float:
+        return max(self.gather(x))
+
+
+def timed_loop(R, stream, ctx, fn, steps, warmup, between=None):
+    """Device time per call of fn(k) on `stream` (CUDA events), the maximum over
+    ranks, with a barrier and a synchronize on both sides. Without `between` the
+    calls run back to back between two events; with it, every call is bracketed
+    by its own events and between() (an L2 flush) runs outside them."""
+    import torch
+    sh = stream.cuda_stream
+    for k in range(warmup):
+        fn(k)
+    ctx.check_status(sh)
+    R.barrier()
+    l0 = ctx.launch_count()
+    if between is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(steps):
+            fn(k)
+        e1.record(stream)
+        R.barrier()
+        ms = e0.elapsed_time(e1) / steps
+    else:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for k in range(steps):
+            between()
+            ev[k][0].record(stream)
+            fn(k)
+            ev[k][1].record(stream)
+        R.barrier()
+        ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    launches = ctx.launch_count() - l0
+    ctx.check_status(sh)
+    per_rank = R.gather(ms)
+    return max(per_rank), per_rank, launches
+
+
+def roofline(alg_bytes, ms, peak_gbs):
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    return round(gbs, 1), round(gbs / peak_gbs, 4)
+
+
 # ------------------------------------------------------------------- ours
 
 def run_ours(args, rank, world, local_rank):
@@ -150,102 +241,78 @@ def run_ours(args, rank, world, local_rank):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", dev))
-
+    R = Ranks(dist, rank, world)
+    peaks = load_peaks()
     shape = DECODE_SHAPES[args.workload]
     Hq, Hk, MAXB = shape["H"], shape["HKV"], shape["max_blocks"]
-    lens, tables, pool_blocks = make_lens_tables(world, args.pool_blocks, shape)
-    B = len(lens)
-    hkv_l, h_l = Hk // world, Hq // world  # this rank's kv-head group
     assert Hk % world == 0, "kv heads must divide over the GPUs"
+    hkv_l, h_l = Hk // world, Hq // world  # this rank's kv-head group
+    n_sets = 1 if world == 1 or args.workload == "c5" else ROTATE
+    lens, tables, pool_blocks = make_lens_tables(shape, n_sets, args.pool_blocks)
+    B = len(lens)
     ctx = zb.GpuContext(dev)
     attn = zb.CudaAttention(ctx)
     stream = torch.cuda.Stream(dev)
+    s_handle = stream.cuda_stream
     g = torch.Generator(device="cuda").manual_seed(SEED + rank)
     with torch.cuda.stream(stream):
         kpool = torch.randn((pool_blocks, hkv_l, BS, D), generator=g, device="cuda").to(torch.bfloat16)
         vpool = torch.randn((pool_blocks, hkv_l, BS, D), generator=g, device="cuda").to(torch.bfloat16)
         q = torch.randn((B, h_l, D), generator=g, device="cuda").to(torch.bfloat16)
         out = torch.empty_like(q)
-        t_tab = torch.from_numpy(tables).cuda()
+        t_tabs = [torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in tables]
         t_len = torch.from_numpy(lens).cuda()
     stream.synchronize()
-    s_handle = stream.cuda_stream
 
-    def step():
-        attn.paged_forward(q, kpool, vpool, t_tab, t_len, out, B, h_l, hkv_l, D, BS, MAXB,
+    def step(k):
+        attn.paged_forward(q, kpool, vpool, t_tabs[k % n_sets], t_len, out, B, h_l, hkv_l, D, BS, MAXB,
                            num_blocks=pool_blocks, stream=s_handle)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---- device-resident timing
-    for _ in range(args.warmup):
-        step()
+    # ---- device-resident timing, clocks sampled over a ~1 s soak and the timed steps
+    for k in range(args.warmup):
+        step(k)
     ctx.check_status(s_handle)
     clocks = ClockSampler(dev)
-    barrier()
+    R.barrier()
     clocks.start()
-    # ~1 s of back-to-back steps so the sampler sees the GPU under this load; the
-    # timed K steps follow immediately, inside the same sampling window.
     t_soak = time.perf_counter()
     while not args.lite and time.perf_counter() - t_soak < 1.0:
-        for _ in range(20):
-            step()
+        for k in range(20):
+            step(k)
         stream.synchronize()
-    barrier()
-    launches0 = ctx.launch_count()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    barrier()
-    dev_ms = e0.elapsed_time(e1)
-    launches = ctx.launch_count() - launches0
+    ms_step, ms_ranks, launches = timed_loop(R, stream, ctx, step, args.steps, 0)
     clk = clocks.stop()
-    ctx.check_status(s_handle)
-    ms_step = max_over_ranks(dev_ms / args.steps)
 
     # ---- end to end through the C ABI with pinned host buffers
     # Every step uploads its inputs (q, block tables, seq_lens packed in one
-    # pinned buffer) and reads its output back. Inputs and outputs are double
-    # buffered on their own copy streams, so the upload of step k+1 and the
-    # readback of step k overlap the kernel of step k, as in a serving loop.
+    # pinned buffer) and reads its output back. Buffers rotate with the table
+    # sets (at least two), each on its own copy streams' events, so the upload
+    # of step k+1 and the readback of step k overlap the kernel of step k, as in
+    # a serving loop.
     from zealot_b200 import lib
     nbytes = lambda t: t.numel() * t.element_size()
-    q_b, tab_b, len_b = nbytes(q), nbytes(t_tab), nbytes(t_len)
+    q_b, tab_b, len_b = nbytes(q), nbytes(t_tabs[0]), nbytes(t_len)
     pack = q_b + tab_b + len_b
     off_tab, off_len = q_b, q_b + tab_b
-    h_in = [torch.empty(pack, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
-    for hb in h_in:
+    n_buf = max(2, n_sets)
+    h_in = [torch.empty(pack, dtype=torch.uint8, pin_memory=True) for _ in range(n_buf)]
+    for i, hb in enumerate(h_in):
         hb[:q_b].copy_(q.cpu().view(torch.uint8).reshape(-1))
-        hb[off_tab:off_len].copy_(torch.from_numpy(tables).view(torch.uint8).reshape(-1))
+        hb[off_tab:off_len].copy_(torch.from_numpy(np.ascontiguousarray(tables[i % n_sets])).view(torch.uint8).reshape(-1))
         hb[off_len:].copy_(torch.from_numpy(lens).view(torch.uint8).reshape(-1))
-    d_in = [torch.empty(pack, dtype=torch.uint8, device="cuda") for _ in range(2)]
-    d_out = [torch.empty_like(out) for _ in range(2)]
-    h_out = [torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    d_in = [torch.empty(pack, dtype=torch.uint8, device="cuda") for _ in range(n_buf)]
+    d_out = [torch.empty_like(out) for _ in range(n_buf)]
+    h_out = [torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_buf)]
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_done = [torch.cuda.Event() for _ in range(2)]
-    ev_free = [torch.cuda.Event() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(n_buf)]
+    ev_done = [torch.cuda.Event() for _ in range(n_buf)]
+    ev_free = [torch.cuda.Event() for _ in range(n_buf)]
     for e in ev_free:
         e.record(s_out)
-    h2d = pack
-    d2h = nbytes(out)
+    h2d, d2h = pack, nbytes(out)
 
     def e2e_step(k):
-        b = k & 1
-        if args.lite:
-            return
+        b = k % n_buf
         with torch.cuda.stream(s_in):
             s_in.wait_event(ev_free[b])          # buffer b's previous kernel and readback are done
             d_in[b].copy_(h_in[b], non_blocking=True)
@@ -262,42 +329,54 @@ def run_ours(args, rank, world, local_rank):
             h_out[b].copy_(d_out[b], non_blocking=True)
             ev_free[b].record(s_out)
 
-    for k in range(args.warmup):
-        e2e_step(k)
-    barrier()
-    l0 = ctx.launch_count()
-    e0.record(s_in)
-    for k in range(args.steps):
-        e2e_step(k)
-    e1.record(s_out)
-    e1.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-    e2e_launches = ctx.launch_count() - l0
-    ctx.check_status(s_handle)
+    e2e = None
+    e2e_launches = 0
     if not args.lite:
-        # the last step's readback equals the device-resident result
-        assert torch.equal(h_out[(args.steps - 1) & 1].view(torch.int16), out.cpu().view(torch.int16))
+        for k in range(args.warmup):
+            e2e_step(k)
+        R.barrier()
+        l0 = ctx.launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s_in)
+        for k in range(args.steps):
+            e2e_step(k)
+        e1.record(s_out)
+        e1.synchronize()
+        R.barrier()
+        e2e_ms = R.max(e0.elapsed_time(e1) / args.steps)
+        e2e_launches = ctx.launch_count() - l0
+        ctx.check_status(s_handle)
+        # the last step's readback equals the device-resident result of the same tables
+        last = (args.steps - 1) % n_buf
+        step(last)
+        stream.synchronize()
+        assert torch.equal(h_out[last].view(torch.int16), out.cpu().view(torch.int16))
+        e2e = {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "zl_paged_decode (C ABI); per step one pinned H2D of q + block tables + seq_lens and "
+                      "a D2H of out per rank, double-buffered on copy streams so transfers overlap the kernel"}
 
     # ---- roofline of the decode kernel (one launch per step)
-    peaks = load_peaks()
     alg = algorithmic_bytes(lens, hkv_l, h_l)
-    achieved = alg / (dev_ms / args.steps * 1e-3) / 1e9
+    achieved, frac = roofline(alg, ms_step, peaks["hbm_gbs"])
     # the committed ncu capture is of the 1-GPU step; other N move different bytes
     traffic = (load_traffic("decode_c2_paged_decode_bf16")
                if world == 1 and args.workload == "decode" else None)
-    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-            "algorithmic_bytes": alg, "peak_source": peaks["source"]}
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": frac,
+            "traffic": traffic, "algorithmic_bytes": alg, "peak_source": peaks["source"],
+            "kernel": "paged_decode_bf16_kernel<4,6,false>"}
+    per_rank = {"ms": [round(x, 5) for x in ms_ranks],
+                "hbm_frac": [roofline(alg, x, peaks["hbm_gbs"])[1] for x in ms_ranks]}
+    del kpool, vpool, d_in, d_out
+    torch.cuda.empty_cache()
 
-    side = {}
-    if rank == 0 and world == 1 and not args.no_side:
-        del kpool, vpool
+    extra = {}
+    if not args.lite and args.workload == "decode":
+        extra.update(measure_c5(args, R, ctx, attn, stream, peaks))
         torch.cuda.empty_cache()
-        side = side_measurements(ctx, attn, stream, peaks, args)
+        extra.update(measure_c3(args, R, ctx, attn, stream, peaks))
+        torch.cuda.empty_cache()
 
-    if dist is not None:
-        dist.barrier()
     if rank == 0:
         tokens_per_s = B / (ms_step * 1e-3)
         if args.workload == "c5":
@@ -305,15 +384,19 @@ def run_ours(args, rank, world, local_rank):
                                "bf16, 8 sequences x 131072 tokens, block_size 16",
                    "global_batch": B, "seq_len": 131072,
                    "parallelism": f"kv-head groups x{world} of the fixed job (rank r: kv heads "
-                                  f"[r*{Hk // world}, (r+1)*{Hk // world})), split-KV inside each GPU",
+                                  f"[r*{hkv_l}, (r+1)*{hkv_l})), split-KV inside each GPU",
                    "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"}
         else:
+            l2 = (f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU" if n_sets == 1 else
+                  f"{alg / 1e6:.0f} MB of KV per step per GPU; steps rotate over {n_sets} block-table sets on "
+                  f"disjoint pool blocks ({n_sets * alg / 1e6:.0f} MB per rotation), so no step re-reads the "
+                  f"previous steps' KV from L2")
             cfg = {"workload": "C2 paged decode, Llama-3-8B layer shape: 32 q / 8 kv heads, head_dim 128, "
                                "bf16, block_size 16, 65536-block pool per GPU",
-                   "global_batch": B, "per_gpu_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
-                   "parallelism": f"kv-head groups x{world} (rank r: kv heads [r*{HKV // world}, "
-                                  f"(r+1)*{HKV // world}))",
-                   "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"}
+                   "global_batch": B, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                   "parallelism": f"kv-head groups x{world} of the fixed 64-sequence job (rank r: kv heads "
+                                  f"[r*{hkv_l}, (r+1)*{hkv_l}) and query heads [r*{h_l}, (r+1)*{h_l}))",
+                   "l2": l2}
         line = {
             "metric": "paged_decode_tokens_per_s",
             "value": round(tokens_per_s, 1),
@@ -323,95 +406,181 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup,
             "ms_per_step": round(ms_step, 5),
             "higher_is_better": True,
-            "scaling": shape["scaling"],
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/K/V, random-permutation block tables)",
             "config": cfg,
-            "hbm_gbs": round(achieved, 1),
-            "hbm_frac": round(achieved / peaks["hbm_gbs"], 4),
-            "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 5),
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "zl_paged_decode (C ABI); per step one pinned H2D of q + block tables + seq_lens and "
-                           "a D2H of out, double-buffered on copy streams so transfers overlap the kernel"},
+            "hbm_gbs": achieved,
+            "hbm_frac": frac,
+            "per_rank": per_rank,
+            "e2e": e2e,
             "gpu_launches": int(launches),
             "e2e_gpu_launches": int(e2e_launches),
             "roofline": roof,
             "clocks": clk,
         }
-        if args.lite:
-            line["e2e"] = None
-        line.update(side)
+        line.update(extra)
         if world == 1 and not args.no_cpu_baseline and args.workload == "decode":
-            line["cpu_baseline"] = cpu_baseline_single(lens, tables)
+            line["cpu_baseline"] = cpu_baseline_single(lens, tables[0])
+            if "prefill" in line:
+                line["prefill"]["cpu_baseline"] = cpu_baseline_prefill()
+            if "reshape_and_cache" in line:
+                line["reshape_and_cache"]["cpu_baseline"] = cpu_baseline_cache()
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist is not None:
+        dist.barrier()
         dist.destroy_process_group()
 
 
-def side_measurements(ctx, attn, stream, peaks, args, only=None):
-    """C3 prefill TFLOPS and reshape_and_cache GB/s (1 GPU, same run)."""
+def measure_c5(args, R, ctx, attn, stream, peaks):
+    """C5 head-sharded at this N, and (N >= 2) the same data split by token range
+    over the ranks and merged with NCCL, with the merged output compared to the
+    head-sharded one."""
     import torch
-    res = {}
-    rng = np.random.default_rng(3)
-    lens = rng.integers(256, 8193, size=16)
+    from zealot_b200.dist import SequenceSplitDecoder, kv_head_group, query_heads_of, token_split
+    shape = DECODE_SHAPES["c5"]
+    rank, world = R.rank, R.world
+    Hq, Hk, MAXB = shape["H"], shape["HKV"], shape["max_blocks"]
+    lens, tables, nb = make_lens_tables(shape, 1, 0)
+    B = len(lens)
+    lo, hi = kv_head_group(rank, world, Hk)
+    hlo, hhi = query_heads_of(lo, hi, Hq, Hk)
+    sh = stream.cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(shape["seed"])  # the same data on every rank
+    with torch.cuda.stream(stream):
+        kf = torch.randn((nb, Hk, BS, D), generator=g, device="cuda").to(torch.bfloat16)
+        vf = torch.randn((nb, Hk, BS, D), generator=g, device="cuda").to(torch.bfloat16)
+        qf = torch.randn((B, Hq, D), generator=g, device="cuda").to(torch.bfloat16)
+        kc = kf if world == 1 else kf[:, lo:hi].contiguous()
+        vc = vf if world == 1 else vf[:, lo:hi].contiguous()
+        qc = qf[:, hlo:hhi].contiguous()
+        oc = torch.empty_like(qc)
+        tt = torch.from_numpy(tables[0]).cuda()
+        tl = torch.from_numpy(lens).cuda()
+    stream.synchronize()
+
+    def head_step(k):
+        attn.paged_forward(qc, kc, vc, tt, tl, oc, B, hhi - hlo, hi - lo, D, BS, MAXB, num_blocks=nb, stream=sh)
+
+    ms, ms_r, _ = timed_loop(R, stream, ctx, head_step, args.steps, args.warmup)
+    alg = algorithmic_bytes(lens, hi - lo, hhi - hlo)
+    res = {"c5": {"workload": "C5: 8 x 131072 tokens, 64 q / 8 kv heads, d 128, bf16; kv heads sharded over "
+                              f"{world} GPU(s) (rank r: kv heads [r*{hi - lo}, (r+1)*{hi - lo})), split-KV inside "
+                              "each GPU; inputs larger than L2",
+                  "tokens_per_s": round(B / (ms * 1e-3), 1), "ms": round(ms, 5),
+                  "hbm_gbs_per_gpu": roofline(alg, ms, peaks["hbm_gbs"])[0],
+                  "hbm_frac": roofline(alg, ms, peaks["hbm_gbs"])[1],
+                  "per_rank": {"ms": [round(x, 5) for x in ms_r],
+                               "hbm_frac": [roofline(alg, x, peaks["hbm_gbs"])[1] for x in ms_r]},
+                  "algorithmic_bytes_per_gpu": alg}}
+    if world > 1:
+        def bcast(x):
+            obj = [x]
+            R.dist.broadcast_object_list(obj, src=0)
+            return obj[0]
+
+        dec = SequenceSplitDecoder(ctx, rank, world, bcast, max_rows=B * Hq, max_head_dim=D, timeout_ms=20000)
+        tb, te = token_split(lens, rank, world, BS)
+        t_tb, t_te = torch.from_numpy(tb).cuda(), torch.from_numpy(te).cuda()
+        os_ = torch.empty((B, Hq, D), dtype=torch.bfloat16, device="cuda")
+        m = torch.empty((B, Hq), dtype=torch.float32, device="cuda")
+        l = torch.empty_like(m)
+        o = torch.empty((B, Hq, D), dtype=torch.float32, device="cuda")
+
+        def partial(k):
+            attn.paged_forward_partial(qf, kf, vf, tt, t_tb, t_te, m, l, o, B, Hq, Hk, D, BS, MAXB,
+                                       num_blocks=nb, stream=sh)
+
+        def split_step(k):
+            dec.decode(qf, kf, vf, tt, t_tb, t_te, os_, Hq, Hk, D, BS, MAXB, num_blocks=nb, stream=sh)
+
+        ms_s, ms_sr, _ = timed_loop(R, stream, ctx, split_step, args.steps, args.warmup)
+        dec.wait()
+        ms_p, ms_pr, _ = timed_loop(R, stream, ctx, partial, args.steps, args.warmup)
+        split_step(0)
+        dec.wait()
+        ctx.check_status(sh)
+        diff = float((os_[:, hlo:hhi].float() - oc.float()).abs().max().item())
+        diff = R.max(diff)
+        dec.close()
+        rng_tokens = (te.astype(np.int64) - tb).sum()
+        alg_s = int(rng_tokens) * Hk * D * 2 * 2 + B * Hq * D * 2 + int(((te + BS - 1) // BS - tb // BS).sum()) * 4
+        gathered = world * B * Hq * (2 + D) * 4
+        res["seq_split"] = {
+            "workload": f"C5 data, each sequence's 131072 tokens split into {world} block-aligned ranges (rank r: "
+                        "tokens [r*L/N, (r+1)*L/N)) over all 64 heads: zl_paged_decode_partial on the local "
+                        "range, then zl_nccl_merge (NCCL all-gather of the (m, l, o) triples over NVLink into "
+                        "local HBM + one merge kernel)",
+            "tokens_per_s": round(B / (ms_s * 1e-3), 1), "ms": round(ms_s, 5),
+            "partial_kernel_ms": round(ms_p, 5), "allgather_and_merge_ms": round(ms_s - ms_p, 5),
+            "hbm_frac_partial_kernel": roofline(alg_s, ms_p, peaks["hbm_gbs"])[1],
+            "gathered_bytes_per_rank": gathered,
+            "max_abs_diff_vs_head_sharded": diff, "tolerance": 2e-2, "parity_ok": diff <= 2e-2,
+            "per_rank": {"ms": [round(x, 5) for x in ms_sr], "partial_ms": [round(x, 5) for x in ms_pr]}}
+    del kf, vf, kc, vc
+    return res
+
+
+def measure_c3(args, R, ctx, attn, stream, peaks):
+    """C3 prefill and reshape_and_cache with this rank's heads; an L2 flush (a
+    256 MB write) runs between timed launches, outside the events."""
+    import torch
+    rank, world = R.rank, R.world
+    h, hkv = H // world, HKV // world
+    lens, rng = c3_lens()
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     T = int(cu[-1])
-    g = torch.Generator(device="cuda").manual_seed(3)
+    sh = stream.cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(C3["seed"] + rank)
     with torch.cuda.stream(stream):
-        q = torch.randn((T, H, D), generator=g, device="cuda").to(torch.bfloat16)
-        k = torch.randn((T, HKV, D), generator=g, device="cuda").to(torch.bfloat16)
-        v = torch.randn((T, HKV, D), generator=g, device="cuda").to(torch.bfloat16)
+        q = torch.randn((T, h, D), generator=g, device="cuda").to(torch.bfloat16)
+        k = torch.randn((T, hkv, D), generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn((T, hkv, D), generator=g, device="cuda").to(torch.bfloat16)
         o = torch.empty_like(q)
         tcu = torch.from_numpy(cu).cuda()
-    sh = stream.cuda_stream
-    flops = sum(4 * H * D * int(L) * (int(L) + 1) / 2 for L in lens)
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream.synchronize()
 
-    def pre():
-        attn.forward_gpu(q, k, v, tcu, o, H, HKV, D, int(lens.max()), causal=True, stream=sh)
+    def between():
+        with torch.cuda.stream(stream):
+            flush.fill_(1.0)
 
-    n = getattr(args, "side_steps", 5)
-    for _ in range(args.warmup if only else 3):
-        if only == "cache":
-            break
-        pre()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if only == "cache":
-        ms = float("nan")
-    else:
-        e0.record(stream)
-        for _ in range(n):
-            pre()
-        e1.record(stream)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / n
-    tf = flops / (ms * 1e-3) / 1e12
-    res["prefill"] = {"workload": "C3 varlen causal prefill: 16 seqs, L U[256,8192], 32/8 heads, d 128, bf16",
-                      "ms": round(ms, 4), "tflops": round(tf, 2), "peak_tflops": peaks["bf16_tflops"],
-                      "frac": round(tf / peaks["bf16_tflops"], 4), "flop": flops}
-    if only == "prefill":
-        ctx.check_status(sh)
-        return res
+    def pre(i):
+        attn.forward_gpu(q, k, v, tcu, o, h, hkv, D, int(lens.max()), causal=True, stream=sh)
+
+    n = max(5, min(args.steps, 20))
+    ms, ms_r, _ = timed_loop(R, stream, ctx, pre, n, 3, between)
+    flop_rank = prefill_flop(lens, h)
+    peak = peaks["bf16_tflops"]
+    tf_r = [flop_rank / (x * 1e-3) / 1e12 for x in ms_r]
+    res = {"prefill": {"workload": f"C3 varlen causal prefill: 16 seqs, L U[256,8192] (T = {T}), 32/8 heads sharded "
+                                   f"over {world} GPU(s) ({h}/{hkv} per GPU), d 128, bf16; L2 flushed between launches",
+                       "ms": round(ms, 4), "tflops": round(world * flop_rank / (ms * 1e-3) / 1e12, 2),
+                       "tflops_per_gpu": round(min(tf_r), 2), "peak_tflops": peak,
+                       "frac": round(min(tf_r) / peak, 4), "flop": world * flop_rank,
+                       "per_rank": {"ms": [round(x, 4) for x in ms_r], "frac": [round(x / peak, 4) for x in tf_r]},
+                       "kernel": "prefill_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators, TMA)"}}
     # reshape_and_cache of the same tokens into a pool via a random slot mapping
     nb = (T + BS - 1) // BS + 64
     with torch.cuda.stream(stream):
-        pk = torch.empty((nb, HKV, BS, D), dtype=torch.bfloat16, device="cuda")
+        pk = torch.empty((nb, hkv, BS, D), dtype=torch.bfloat16, device="cuda")
         pv = torch.empty_like(pk)
         slots = torch.from_numpy(rng.permutation(nb * BS)[:T].astype(np.int64)).cuda()
-    for _ in range(args.warmup if only else 3):
-        attn.reshape_and_cache(k, v, pk, pv, slots, HKV, D, BS, nb, stream=sh)
-    e0.record(stream)
-    for _ in range(n):
-        attn.reshape_and_cache(k, v, pk, pv, slots, HKV, D, BS, nb, stream=sh)
-    e1.record(stream)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / n
-    byts = 2 * (T * HKV * D * 2) * 2 + 8 * T
-    res["reshape_and_cache"] = {"workload": f"C3 tokens ({T}) x 8 kv heads x 128 bf16, random slots",
-                                "ms": round(ms, 4), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
-                                "frac": round(byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
-    ctx.check_status(sh)
+    stream.synchronize()
+
+    def cache(i):
+        attn.reshape_and_cache(k, v, pk, pv, slots, hkv, D, BS, nb, stream=sh)
+
+    ms, ms_r, _ = timed_loop(R, stream, ctx, cache, n, 3, between)
+    byts = 2 * (T * hkv * D * 2) * 2 + 8 * T
+    res["reshape_and_cache"] = {
+        "workload": f"C3 tokens ({T}) x {hkv} kv heads per GPU x 128 bf16, random slots; L2 flushed between launches",
+        "ms": round(ms, 4), "gbs_per_gpu": roofline(byts, ms, peaks["hbm_gbs"])[0],
+        "frac": roofline(byts, ms, peaks["hbm_gbs"])[1], "bytes_per_gpu": byts,
+        "per_rank": {"ms": [round(x, 4) for x in ms_r]}}
+    del q, k, v, o, pk, pv, flush
     return res
 
 
@@ -423,12 +592,12 @@ def run_side_only(args):
     ctx = zb.GpuContext(0)
     attn = zb.CudaAttention(ctx)
     stream = torch.cuda.Stream(0)
-    args.side_steps = args.steps
-    res = side_measurements(ctx, attn, stream, load_peaks(), args, only=args.workload)
+    R = Ranks(None, 0, 1)
+    res = measure_c3(args, R, ctx, attn, stream, load_peaks())
     key = "prefill" if args.workload == "prefill" else "reshape_and_cache"
     r = res[key]
     line = {"metric": "prefill_tflops" if key == "prefill" else "reshape_and_cache_gbs",
-            "value": r["tflops"] if key == "prefill" else r["gbs"],
+            "value": r["tflops"] if key == "prefill" else r["gbs_per_gpu"],
             "unit": "TFLOP/s" if key == "prefill" else "GB/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "dtype": "bf16",
             "config": {"workload": r["workload"]}, "detail": r}
@@ -732,6 +901,57 @@ def _oracle_inputs(lens, tables, hkv, h, n_seqs):
     return q, kp, vp, t2, lens
 
 
+def cpu_baseline_prefill():
+    """The oracle's causal prefill (CpuAttention rows, src/attention/mod.rs:31-103),
+    one thread, on a seeded subset of C3 (sequences 1 and 2, one query head and its
+    kv head), scaled to the whole C3 job by exact FLOP: extrapolated."""
+    from oracle import oracle
+    lens, _ = c3_lens()
+    sub = [int(lens[1]), int(lens[2])]
+    rng = np.random.default_rng(C3["seed"] + 7)
+    T = sum(sub)
+    cu = np.array([0, sub[0], T], np.int32)
+    q, k, v = (oracle.round_bf16(rng.standard_normal((T, 1, D)).astype(np.float32)) for _ in range(3))
+    t0, reps = time.perf_counter(), 0
+    while True:
+        oracle.prefill_varlen(q, k, v, cu, 1, 1, D, causal=True, num_threads=1)
+        reps += 1
+        if time.perf_counter() - t0 > 3.0:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    tflops = prefill_flop(sub, 1) / dt / 1e12
+    job_s = prefill_flop(lens, H) / (tflops * 1e12)
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "job_s_extrapolated": round(job_s, 1),
+            "sample": f"C3 sequences 1-2 (L = {sub[0]}, {sub[1]}), 1 head, {reps} repetitions of {dt:.2f} s; "
+                      "scaled to the 16-sequence, 32-head job by exact FLOP (extrapolated); oracle/zl_oracle.c"}
+
+
+def cpu_baseline_cache():
+    """The oracle's store_kv offset arithmetic (src/kv_cache.rs:212-276), one thread,
+    on 8192 of the C3 tokens with all 8 kv heads; GB/s of the same byte model."""
+    from oracle import oracle
+    rng = np.random.default_rng(C3["seed"] + 8)
+    T = 8192
+    nb = T // BS + 64
+    k = oracle.round_bf16(rng.standard_normal((T, HKV, D)).astype(np.float32))
+    v = oracle.round_bf16(rng.standard_normal((T, HKV, D)).astype(np.float32))
+    kp = np.zeros((nb, HKV, BS, D), np.float32)
+    vp = np.zeros_like(kp)
+    slots = rng.permutation(nb * BS)[:T].astype(np.int64)
+    t0, reps = time.perf_counter(), 0
+    while True:
+        oracle.reshape_and_cache(kp, vp, k, v, slots, HKV, D, BS, nb)
+        reps += 1
+        if time.perf_counter() - t0 > 2.0:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    byts = 2 * (T * HKV * D * 2) * 2 + 8 * T  # the GPU's bf16 byte model for the same tokens
+    return {"value": round(byts / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{T} C3 tokens x 8 kv heads, {reps} repetitions of {dt * 1e3:.1f} ms; byte model of the bf16 "
+                      "GPU call (the oracle copies fp32 rows); oracle/zl_oracle.c"}
+
+
 def cpu_baseline_single(lens, tables):
     """The oracle port, single-threaded like the reference CpuAttention, on a sample of
     the C2 step (the first 16 of 64 sequences, all heads); scaled to tokens/s."""
@@ -757,7 +977,8 @@ def run_reference(args, rank, world):
         return
     from oracle import oracle
     cores = os.cpu_count() or 1
-    lens, tables, _ = make_lens_tables(world)
+    lens, tables, _ = make_lens_tables()
+    tables = tables[0]
     B = len(lens)
     hkv, h = HKV, H  # the whole job's heads: the CPU does every shard's work
     n = min(B, 64)
@@ -771,7 +992,7 @@ def run_reference(args, rank, world):
     val = n / dt
     line = {"impl": "reference", "metric": "paged_decode_tokens_per_s", "value": round(val, 2),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) bf16-rounded q/K/V, U[512,4096] contexts)",
             "config": {"workload": "C2 paged decode, Llama-3-8B layer shape (CPU reference path)",
@@ -790,7 +1011,6 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-side", action="store_true", help="skip the prefill / cache side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["decode", "c5", "prefill", "cache", "c4", "decode-loop"],
                     default="decode",
@@ -811,7 +1031,7 @@ def main():
     if args.gpus != world:
         log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; running {world} rank(s)")
     if args.lite:
-        args.no_side = args.no_cpu_baseline = True
+        args.no_cpu_baseline = True
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
@@ -823,8 +1043,6 @@ def main():
             raise SystemExit(f"--workload {args.workload} runs on one GPU")
         (run_c4 if args.workload == "c4" else run_decode_loop)(args)
         return
-    if args.workload == "c5":
-        args.no_side = True
     run_ours(args, rank, world, local_rank)
 
 

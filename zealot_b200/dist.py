@@ -137,6 +137,7 @@ class SequenceSplitDecoder:
         peer that is gone."""
         self.ctx, self.lib, self.rank, self.world = ctx, ctx.lib, rank, world
         self.watch, self._step = watch, 0
+        self._parts = {}
         buf = (ctypes.c_uint8 * 128)()
         if rank == 0:
             check(self.lib.zl_nccl_get_unique_id(buf))
@@ -155,9 +156,14 @@ class SequenceSplitDecoder:
             self.watch.step(self._step)
             self._step += 1
         B = tok_end.numel()
-        m = torch.empty((B, num_heads), dtype=torch.float32, device=q.device)
-        l = torch.empty_like(m)
-        o = torch.empty((B, num_heads, head_dim), dtype=torch.float32, device=q.device)
+        # the partial triples live as long as the decoder (no allocation per step,
+        # and never memory the caching allocator could hand to another stream)
+        key = (B, num_heads, head_dim, q.device)
+        if key not in self._parts:
+            m = torch.empty((B, num_heads), dtype=torch.float32, device=q.device)
+            self._parts[key] = (m, torch.empty_like(m),
+                                torch.empty((B, num_heads, head_dim), dtype=torch.float32, device=q.device))
+        m, l, o = self._parts[key]
         if num_blocks is None:
             num_blocks = k_pool.numel() // (block_size * num_kv_heads * head_dim)
         st = self.ctx.stream(stream)
