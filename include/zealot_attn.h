@@ -75,6 +75,18 @@ typedef struct {
  * creates the library state. cfg may be NULL (device 0). */
 zl_status zl_ctx_create(const zl_ctx_cfg* cfg, zl_ctx** out);
 zl_status zl_ctx_destroy(zl_ctx* ctx);
+/* Context flags (zl_ctx_set_flags). No reference counterpart.
+ * ZL_CTX_INPUTS_AHEAD: the block tables, seq_lens and token ranges passed to
+ * decode calls on this context are written (e.g. copied from the host) before
+ * the kernel that precedes the decode on its stream starts. The decode kernel
+ * is launched with programmatic stream serialization in any case -- its CTAs
+ * may become resident while that kernel finishes -- and with this flag it
+ * also scans the lengths and reads its first table entries before waiting for
+ * that kernel; q, the pools and every output are touched only after the wait.
+ * Leave it off when the preceding kernel writes the tables or lengths (a
+ * device-side block-table update). */
+#define ZL_CTX_INPUTS_AHEAD 1u
+zl_status zl_ctx_set_flags(zl_ctx* ctx, uint32_t flags);
 /* Thread-local text of the last error returned on this thread. */
 const char* zl_last_error(void);
 const char* zl_status_string(zl_status s);

@@ -71,6 +71,7 @@ class zl_sampling_params(ctypes.Structure):
 # name -> (restype, argtypes); every symbol declared in include/zealot_attn.h
 SIGNATURES = {
     "zl_ctx_create": (c_int, [P(zl_ctx_cfg), P(c_void_p)]),
+    "zl_ctx_set_flags": (c_int, [c_void_p, ctypes.c_uint32]),
     "zl_ctx_destroy": (c_int, [c_void_p]),
     "zl_last_error": (c_char_p, []),
     "zl_status_string": (c_char_p, [c_int]),

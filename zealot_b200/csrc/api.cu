@@ -125,6 +125,13 @@ zl_status zl_ctx_create(const zl_ctx_cfg* cfg, zl_ctx** out) {
   return ZL_OK;
 }
 
+zl_status zl_ctx_set_flags(zl_ctx* ctx, uint32_t flags) {
+  if (!ctx) return set_error(ZL_ERR_INVALID_ARG, "null context");
+  if (flags & ~ZL_CTX_INPUTS_AHEAD) return set_error(ZL_ERR_INVALID_ARG, "unknown context flags 0x%x", flags);
+  ctx->flags = flags;
+  return ZL_OK;
+}
+
 zl_status zl_nccl_finalize(zl_ctx* ctx);
 
 zl_status zl_ctx_destroy(zl_ctx* ctx) {

@@ -62,6 +62,10 @@ struct DecodeArgs {
                                // all zero on entry and exit except the barrier generation
   int* status;
   int B, H, Hkv, G, max_blocks;
+  // 1: block_tables / seq_lens / tok_begin are complete before the previous
+  // kernel on the stream starts, so they are read before the dependency wait;
+  // 0: nothing is read before it.
+  int inputs_ahead;
   int64_t num_blocks;
   float scale_log2;            // scale * log2(e)
 };
@@ -73,9 +77,10 @@ struct Smem {
   static constexpr int kInfo = WARPS * STAGES * 4;
   static constexpr int kPrefix = (MAX_B + 1) * 4;
   static constexpr int kJbase = PARTIAL ? MAX_B * 4 : 0;  // table index of each range's first block
-  static constexpr int kTotal = 1024 /*alignment slack*/ + kRing + kBars + kInfo + kPrefix + kJbase + 16;
+  static constexpr int kParts = (kRing + kBars + kInfo + kPrefix + kJbase + 15) & ~15;
+  static constexpr int kPartBytes = WARPS * (2 * MAX_G + MAX_G * D) * 4;  // the warps' staged shares
+  static constexpr int kTotal = 1024 /*alignment slack*/ + kParts + kPartBytes;
 };
-static_assert(Smem<4, 6, true>::kTotal <= 232448, "shared memory of the partial form");
 
 // Blocks of sequence b's token range and the block-table index of its first
 // block. The normalised form attends to [0, seq_lens[b]); the partial form to
@@ -97,16 +102,6 @@ __device__ __forceinline__ int range_blocks(const DecodeArgs& a, int b, int& jt0
 // tile: two 2 KB boxes of [16 rows][64 cols], 128-byte swizzle (chunk ^= row%8).
 __device__ __forceinline__ uint32_t tile_off(int r, int c) {
   return (uint32_t)((c >> 3) * 2048 + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
-}
-
-// A split (sequence, kv head) with more contributor warps than this is merged
-// after a grid barrier by several warps instead of by its last contributor.
-constexpr int kMaxLastArriver = 16;
-
-// Warp index owning flat block x when TB blocks are split over W warps as
-// [gw*TB/W, (gw+1)*TB/W).
-__device__ __forceinline__ int owner_warp(int64_t x, int64_t TB, int64_t W) {
-  return (int)(((x + 1) * W - 1) / TB);
 }
 
 // Whether any of the n int32 entries at p is negative; all `nthreads` threads
@@ -148,46 +143,191 @@ __device__ __forceinline__ void emit_merged(const DecodeArgs& a, int64_t row, in
   }
 }
 
-// Grid-wide barrier of a cooperative launch (all CTAs co-resident). words[0]
-// counts arrivals and is reset by the last CTA, which then bumps words[1]
-// (the generation) that the others wait on. The wait is bounded and gives up
-// when another CTA has reported a timeout.
-__device__ bool grid_barrier(int* words, int* status) {
-  __shared__ int ok_s;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    volatile int* gen = words + 1;
-    const int g = *gen;
-    __threadfence();
-    int ok = 1;
-    if (atomicAdd(words, 1) + 1 == (int)gridDim.x) {
-      atomicExch(words, 0);
-      __threadfence();
-      atomicAdd(words + 1, 1);
-    } else {
-      const long long t0 = clock64();
-      while (*gen == g) {
-        __nanosleep(64);
-        if (aborted(status)) { ok = 0; break; }
-        if (clock64() - t0 > kWaitCycles) {
-          atomicOr(status, 2 /* ZL_DEV_TIMEOUT */);
-          ok = 0;
-          break;
+// Warp partial of one (sequence, kv head) segment, staged in shared memory for
+// the CTA's combine: m in natural-log units, l and o relative to it.
+struct WarpPart {
+  float m[MAX_G];
+  float l[MAX_G];
+  float o[MAX_G][D];
+};
+
+// Unit (warp or CTA) owning flat block x when the flat list is split into
+// contiguous ranges of `per` or `per + 1` blocks (the first `rem` units take
+// one more).
+__device__ __forceinline__ int owner_unit(int x, int per, int rem) {
+  const int big = rem * (per + 1);
+  return x < big ? x / (per + 1) : rem + (x - big) / per;
+}
+__device__ __forceinline__ int unit_start(int u, int per, int rem) { return u * per + min(u, rem); }
+
+// Named barrier over the CTA's WARPS warps (id 1; __syncthreads is id 0).
+template <int WARPS>
+__device__ __forceinline__ void cta_bar() {
+  asm volatile("bar.sync 1, %0;" ::"r"(WARPS * 32) : "memory");
+}
+
+// Per-warp ranges are used while a segment spreads over fewer than
+// kGroupAvgContrib warps on average and over at most kMaxWarpContrib warps;
+// beyond that the CTA's warps share one range (fewer, larger merges). Measured
+// on B200 (C2 shapes): per-warp ranges win at about 2-3 contributors per
+// segment, CTA ranges from about 5.
+constexpr int kGroupAvgContrib = 4;
+constexpr int kMaxWarpContrib = 16;
+
+// Merges the partial triples of `nc` consecutive units for head n of a split
+// segment (m natural-log, l, o relative to m) and emits the row; one warp.
+template <bool PARTIAL, typename SlotOf>
+__device__ __forceinline__ void merge_units(const DecodeArgs& a, int64_t row, int n, int nc, int lane,
+                                            SlotOf slot_of) {
+  float M = -INFINITY;
+  for (int k0 = 0; k0 < nc; k0 += 32)
+    if (k0 + lane < nc) M = fmaxf(M, __ldcg(&slot_of(k0 + lane)->m[n]));
+#pragma unroll
+  for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float den = 0.f;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < nc; k0 += 32) {
+    float wl = 0.f;
+    if (k0 + lane < nc) {
+      const Partial* pc = slot_of(k0 + lane);
+      const float mc = __ldcg(&pc->m[n]);
+      wl = (mc == -INFINITY) ? 0.f : __expf(mc - M);
+      den += wl * __ldcg(&pc->l[n]);
+    }
+    const int cnt = min(32, nc - k0);
+    for (int u0 = 0; u0 < cnt; u0 += 8) {
+      float4 x[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++)  // eight rows in flight
+        x[u] = (u0 + u < cnt) ? __ldcg(reinterpret_cast<const float4*>(slot_of(k0 + u0 + u)->o[n]) + lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const float w = __shfl_sync(0xffffffffu, wl, (u0 + u) & 31);
+        if (u0 + u < cnt) {
+          num.x += w * x[u].x; num.y += w * x[u].y; num.z += w * x[u].z; num.w += w * x[u].w;
         }
       }
     }
-    __threadfence();
-    ok_s = ok;
   }
-  __syncthreads();
-  return ok_s != 0;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  emit_merged<PARTIAL>(a, row, lane, M, den, num);
+}
+
+// The same merge for all G heads of the segment at once (one warp): lane c
+// holds contributor c's (m, l) for every head, and the rows of contributors 0
+// and 1 are loaded in the same round, so a split over two contributors (the
+// common case of per-warp ranges) costs one L2 round trip before the math.
+template <bool PARTIAL, typename SlotOf>
+__device__ __forceinline__ void merge_units_all(const DecodeArgs& a, int64_t row0, int G, int nc, int lane,
+                                                SlotOf slot_of) {
+  float M[MAX_G], den[MAX_G], mc[MAX_G], lc[MAX_G];
+  float4 x1[MAX_G], x2[MAX_G];
+  {
+    const bool mine = lane < nc;
+    const Partial* pc = slot_of(mine ? lane : 0);
+    const float4* o1 = reinterpret_cast<const float4*>(&slot_of(0)->o[0][0]) + lane;
+    const float4* o2 = reinterpret_cast<const float4*>(&slot_of(nc > 1 ? 1 : 0)->o[0][0]) + lane;
+#pragma unroll
+    for (int n = 0; n < MAX_G; n++) {
+      mc[n] = -INFINITY;
+      lc[n] = 0.f;
+      if (n < G) {
+        if (mine) { mc[n] = __ldcg(&pc->m[n]); lc[n] = __ldcg(&pc->l[n]); }
+        x1[n] = __ldcg(o1 + n * (D / 4));
+        x2[n] = __ldcg(o2 + n * (D / 4));
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < MAX_G; n++) { M[n] = mc[n]; den[n] = 0.f; }
+  // contributors past 32 (very long sequences): their maxima too
+  for (int c0 = 32; c0 < nc; c0 += 32)
+    if (c0 + lane < nc) {
+      const Partial* pc = slot_of(c0 + lane);
+#pragma unroll
+      for (int n = 0; n < MAX_G; n++)
+        if (n < G) M[n] = fmaxf(M[n], __ldcg(&pc->m[n]));
+    }
+#pragma unroll
+  for (int n = 0; n < MAX_G; n++)
+#pragma unroll
+    for (int off = 16; off; off >>= 1) M[n] = fmaxf(M[n], __shfl_xor_sync(0xffffffffu, M[n], off));
+  float4 num[MAX_G];
+#pragma unroll
+  for (int n = 0; n < MAX_G; n++) num[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = 0; c0 < nc; c0 += 32) {
+    float wl[MAX_G];
+    if (c0 + lane < nc) {
+      const Partial* pc = slot_of(c0 + lane);
+#pragma unroll
+      for (int n = 0; n < MAX_G; n++) {
+        wl[n] = 0.f;
+        if (n < G) {
+          const float m_ = c0 == 0 ? mc[n] : __ldcg(&pc->m[n]);
+          const float l_ = c0 == 0 ? lc[n] : __ldcg(&pc->l[n]);
+          wl[n] = (m_ == -INFINITY) ? 0.f : __expf(m_ - M[n]);
+          den[n] += wl[n] * l_;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < MAX_G; n++) wl[n] = 0.f;
+    }
+    const int cnt = min(32, nc - c0);
+    for (int k = 0; k < cnt; k += 2) {
+      const bool second = k + 1 < cnt;
+      if (c0 + k > 0) {  // rows of contributors 0 and 1 are already loaded
+        const float4* o1 = reinterpret_cast<const float4*>(&slot_of(c0 + k)->o[0][0]) + lane;
+        const float4* o2 = reinterpret_cast<const float4*>(&slot_of(c0 + k + (second ? 1 : 0))->o[0][0]) + lane;
+#pragma unroll
+        for (int n = 0; n < MAX_G; n++) {
+          if (n < G) {
+            x1[n] = __ldcg(o1 + n * (D / 4));
+            x2[n] = __ldcg(o2 + n * (D / 4));
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < MAX_G; n++) {
+        const float w1 = __shfl_sync(0xffffffffu, wl[n], k);
+        const float w2 = second ? __shfl_sync(0xffffffffu, wl[n], k + 1) : 0.f;
+        if (n < G) {
+          num[n].x += w1 * x1[n].x + w2 * x2[n].x;
+          num[n].y += w1 * x1[n].y + w2 * x2[n].y;
+          num[n].z += w1 * x1[n].z + w2 * x2[n].z;
+          num[n].w += w1 * x1[n].w + w2 * x2[n].w;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < MAX_G; n++) {
+#pragma unroll
+    for (int off = 16; off; off >>= 1) den[n] += __shfl_xor_sync(0xffffffffu, den[n], off);
+    if (n < G) emit_merged<PARTIAL>(a, row0 + n, lane, M[n], den[n], num[n]);
+  }
 }
 
 // PARTIAL = false: normalised bf16 output over [0, seq_lens[b]).
 // PARTIAL = true: the unnormalised triple (m, l, o) of each (sequence, head)
 // over the token range [tok_begin[b], seq_lens[b]), m being the true maximum
 // score (the sequence-split form, merged across GPUs afterwards).
+//
+// Work split. The flat list of (sequence, kv head, 16-token block) in
+// (b, kvh, j) order is cut into equal contiguous ranges, one per unit
+// ("stream-K" at block granularity, so ragged contexts cost no imbalance). The
+// kernel picks the unit from the job it finds (the same choice in every CTA):
+//  * per-warp ranges for long jobs: warps stream independently; a segment
+//    (sequence, kv head) inside one warp's range is written out directly, a
+//    segment spanning warps leaves one partial per warp and the last warp to
+//    finish merges them;
+//  * per-CTA ranges for short jobs: warp w of a CTA takes blocks w, w + WARPS,
+//    ... of the CTA's range, at each segment end the warps' partials are
+//    combined through shared memory (CTA barrier), and a segment spanning CTAs
+//    is merged by the last CTA to finish it -- a few large merges instead of
+//    many small ones.
 template <int WARPS, int STAGES, bool PARTIAL>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tmK,
@@ -201,28 +341,39 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   int* info = reinterpret_cast<int*>(base + SM::kRing + SM::kBars);
   int* prefix = reinterpret_cast<int*>(base + SM::kRing + SM::kBars + SM::kInfo);
   int* jbase = reinterpret_cast<int*>(base + SM::kRing + SM::kBars + SM::kInfo + SM::kPrefix);
+  WarpPart* wpart = reinterpret_cast<WarpPart*>(base + SM::kParts);
+  __shared__ int s_last;
+  __shared__ int s_max_nb;    // longest sequence in blocks
+  __shared__ int s_nonempty;  // sequences with at least one block
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int B = a.B, Hkv = a.Hkv;
 
-  if (aborted(a.status)) return;  // an earlier launch timed out and was not cleared
+  // Programmatic dependent launch: the next kernel may be scheduled now; this
+  // one waits for its predecessor before the first read of anything that
+  // kernel could write (at once, unless the caller declared the tables and
+  // lengths ready ahead: then after the prologue and the first table reads).
+  griddep_launch_dependents();
+  if (!a.inputs_ahead) griddep_wait();
+  // An earlier launch timed out and was not cleared: return, the whole CTA
+  // alike (its warps may meet at CTA barriers further on).
+  if (__syncthreads_or(aborted(a.status))) return;
   if (tid == 0) {
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
+    s_max_nb = 0;
+    s_nonempty = 0;
   }
   for (int i = tid; i < WARPS * STAGES; i += blockDim.x) mbar_init(smem_u32(&bars[i]), 1);
-  __shared__ int s_max_nb;  // longest sequence in blocks
-  if (tid == 0) s_max_nb = 0;
-  __syncthreads();
 
-  // ---- per-CTA prologue: prefix[b] = Hkv * sum_{b'<b} nblk(b') (flat start of b)
+  // ---- per-CTA prologue: prefix[b] = sum_{b'<b} nblk(b') (flat start of b is Hkv * prefix[b])
   {
     constexpr int T = WARPS * 32;
     const int per = (B + T - 1) / T;
     const int b0 = tid * per;
-    int local = 0, lmax = 0;
+    int local = 0, lmax = 0, lcount = 0;
     for (int k = 0; k < per; k++) {
       const int b = b0 + k;
       if (b < B) {
@@ -233,18 +384,22 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         if (PARTIAL) jbase[b] = jt0;
         local += nb;
         lmax = max(lmax, nb);
+        lcount += nb > 0;
       }
     }
-    if (lmax > 0) atomicMax(&s_max_nb, lmax);
     // block-wide exclusive scan of `local`
     int incl = local;
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += v;
     }
-    __shared__ int warp_tot[WARPS];  // (s_max_nb was zeroed before the barrier above)
+    __shared__ int warp_tot[WARPS];
     if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
+    __syncthreads();  // (also orders s_max_nb = 0 before the atomicMax below)
+    if (lmax > 0) {
+      atomicMax(&s_max_nb, lmax);
+      atomicAdd(&s_nonempty, lcount);
+    }
     int run = incl - local;
     for (int w = 0; w < warp; w++) run += warp_tot[w];
     if (tid == 0) prefix[0] = 0;
@@ -261,17 +416,12 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   fence_mbar_init();
   __syncthreads();
 
-  const int64_t NB = prefix[B];         // sum of blocks over sequences
-  const int64_t TB = NB * Hkv;          // flat work items
-  // Active warps: never more than work items, so every warp in [0, W) owns at
-  // least one block and the contributors of a split (sequence, kv head) are
-  // exactly the consecutive warps owner_warp(first block) .. owner_warp(last).
-  const int64_t W = min((int64_t)gridDim.x * WARPS, TB);
-  const int gw = blockIdx.x * WARPS + warp;
+  const int TB = prefix[B] * Hkv;  // flat work items (< 2^31, checked on the host)
 
   // Sequences with no context produce zeros, (-inf, 0, 0) in the partial
   // form (CTA 0 writes them).
   if (blockIdx.x == 0) {
+    griddep_wait();
     for (int b = warp; b < B; b += WARPS) {
       if (prefix[b + 1] == prefix[b]) {
         if constexpr (PARTIAL) {
@@ -292,35 +442,44 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   }
   if (TB == 0) return;
 
-  // Merge mode, the same in every CTA: when every split (sequence, kv head)
-  // has few contributor warps, the last one to finish merges it (no global
-  // wait); when a long sequence spreads over many warps, all warps meet at a
-  // grid barrier and the merges are spread over the contributors.
-  bool barrier_mode = false;
-  if (TB > 0) {
-    const int64_t per_warp = TB / W;  // >= 1
-    const int max_nb = s_max_nb;
-    barrier_mode = (max_nb + per_warp - 1) / per_warp + 1 > kMaxLastArriver;
+  // ---- the unit of the split, the same in every CTA
+  const int nwarps = (int)gridDim.x * WARPS;
+  bool grouped;
+  {
+    const int per_warp = TB / min(nwarps, TB);
+    const int avg_nb = prefix[B] / max(s_nonempty, 1);
+    grouped = avg_nb >= (kGroupAvgContrib - 1) * per_warp ||
+              (s_max_nb + per_warp - 1) / per_warp + 1 > kMaxWarpContrib;
   }
-  // Warps past W own nothing but still take part in the grid barrier below.
-  const int64_t f0 = gw < W ? (int64_t)gw * TB / W : TB;
-  const int64_t f1 = gw < W ? (int64_t)(gw + 1) * TB / W : TB;
-  const int nwork = (int)(f1 - f0);
+  // Active units: never more than work items, so every active unit owns at
+  // least one block and the contributors of a split segment are the
+  // consecutive units owner_unit(first block) .. owner_unit(last block).
+  const int U = min(grouped ? (int)gridDim.x : nwarps, TB);
+  const int unit = grouped ? (int)blockIdx.x : (int)blockIdx.x * WARPS + warp;
+  if (grouped && unit >= U) return;  // uniform over the CTA
+  const int uper = TB / U, urem = TB - uper * U;
+  const bool active = unit < U;      // per-warp: warps past U own nothing
+  const int u0 = active ? unit_start(unit, uper, urem) : TB;
+  const int u1 = active ? u0 + uper + (unit < urem ? 1 : 0) : TB;
+  // this warp's items: flat blocks u0 + ioff + istride * k, k in [0, nwork)
+  const int istride = grouped ? WARPS : 1, ioff = grouped ? warp : 0;
+  const int nwork = u1 - u0 > ioff ? (u1 - u0 - ioff + istride - 1) / istride : 0;
+  auto item_flat = [&](int k) { return u0 + ioff + istride * k; };
 
-  // Locate flat index f0: sequence b (largest with Hkv*prefix[b] <= f0).
-  auto locate = [&](int64_t f, int& b, int& kvh, int& j) {
+  // Segment of flat block f: sequence b (largest with Hkv*prefix[b] <= f), kv
+  // head and block index j inside the segment.
+  auto locate = [&](int f, int& b, int& kvh, int& j) {
     int lo = 0, hi = B;  // Hkv*prefix[lo] <= f < Hkv*prefix[hi]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if ((int64_t)prefix[mid] * Hkv <= f) lo = mid; else hi = mid;
+      if (prefix[mid] * Hkv <= f) lo = mid; else hi = mid;
     }
-    // skip empty sequences (prefix equal)
-    while ((int64_t)prefix[lo + 1] * Hkv <= f) lo++;
+    while (prefix[lo + 1] * Hkv <= f) lo++;  // skip empty sequences (prefix equal)
     b = lo;
     const int nb = prefix[b + 1] - prefix[b];
-    const int64_t off = f - (int64_t)prefix[b] * Hkv;
-    kvh = (int)(off / nb);
-    j = (int)(off - (int64_t)kvh * nb);
+    const int off = f - prefix[b] * Hkv;
+    kvh = off / nb;
+    j = off - kvh * nb;
   };
 
   // Partial form: a negative table entry before a range's start ends the
@@ -328,12 +487,13 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   // entries [0, jbase[b]) of every sequence its warps touch, once, and marks a
   // sequence so found in the sign bit of jbase[b].
   if constexpr (PARTIAL) {
-    const int64_t gw0 = (int64_t)blockIdx.x * WARPS;
-    if (gw0 < W) {  // uniform over the CTA
-      const int64_t gw1 = min(gw0 + WARPS, W);
+    const int f_lo = grouped ? u0 : unit_start(blockIdx.x * WARPS, uper, urem);
+    const int w_hi = min((int)(blockIdx.x + 1) * WARPS, U);
+    const int f_hi = grouped ? u1 : (w_hi > (int)blockIdx.x * WARPS ? unit_start(w_hi, uper, urem) : f_lo);
+    if (f_hi > f_lo) {  // uniform over the CTA
       int bl, bh, k_, j_;
-      locate(gw0 * TB / W, bl, k_, j_);
-      locate(gw1 * TB / W - 1, bh, k_, j_);
+      locate(f_lo, bl, k_, j_);
+      locate(f_hi - 1, bh, k_, j_);
       for (int b = bl; b <= bh; b++) {
         const int n = jbase[b];
         bool neg = false;
@@ -346,26 +506,28 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   auto table_base = [&](int b) -> int { return PARTIAL ? (jbase[b] & 0x7fffffff) : 0; };
   auto cut_before = [&](int b) -> bool { return PARTIAL && jbase[b] < 0; };
 
-  if (nwork > 0) {
   const uint32_t ring = base_u32 + warp * STAGES * STAGE;
   uint64_t* wbars = bars + warp * STAGES;
   int* winfo = info + warp * STAGES;
   const uint64_t policy = policy_evict_first();
 
-  // ---------------- producer: block list in chunks of 32 (warp-wide) ----------------
-  // Every 32 blocks the whole warp resolves the next 32 entries of its range
-  // at once (one coalesced table read, one seq_lens read per lane): lane L
-  // holds the TMA row and valid-token count of block ch_base + L. A negative
-  // table entry ends its sequence (paged_attention.cu:66-67): a block is
-  // dropped when any entry at or before it in the same (sequence, kv head)
-  // is negative, tracked across chunks by carry_seg / carry_trunc.
+  // ---------------- producer: item list in chunks of 32 (warp-wide) ----------------
+  // Every 32 items the whole warp resolves the next 32 at once: lane L holds
+  // the TMA row and the valid tokens of item ch_base + L. A negative table
+  // entry ends its sequence (paged_attention.cu:66-67): a block is dropped when
+  // any entry at or before it in the same sequence is negative. Each lane
+  // checks its own entry and, in the CTA split, the WARPS - 1 entries before
+  // it (the blocks the CTA's other warps take), so the lanes' windows tile the
+  // table; the ballot carries the result along the chunk and carry_seg /
+  // carry_trunc across chunks, and the first item's earlier entries are
+  // scanned once.
   const int32_t* const tables = a.block_tables;
   int ch_base = -32, ch_y = 0, ch_nv = 0;
-  int carry_seg, carry_trunc;
-  {
+  int carry_seg = -1, carry_trunc = 0;
+  if (nwork > 0) {
     int b, kvh, j;
-    locate(f0, b, kvh, j);
-    const int t_lo = table_base(b);  // entries before the range: cut_before(b)
+    locate(item_flat(0), b, kvh, j);
+    const int t_lo = table_base(b);
     j += t_lo;
     bool neg = cut_before(b);
     const int32_t* tb = tables + (int64_t)b * a.max_blocks;
@@ -384,19 +546,25 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     carry_trunc = __any_sync(0xffffffffu, neg) ? 1 : 0;
     carry_seg = b * Hkv + kvh;
   }
-  auto build_chunk = [&](int base) {
-    const int idx = base + lane;
+  auto build_chunk = [&](int cbase) {
+    const int idx = cbase + lane;
     const bool ok = idx < nwork;
     int seg = -1, e = 0, b = 0, kvh = 0, j = 0, len = 0, beg = 0;
+    bool wneg = false;
     if (ok) {
-      locate(f0 + idx, b, kvh, j);
+      locate(item_flat(idx), b, kvh, j);
       seg = b * Hkv + kvh;
-      j += table_base(b);  // j: table index from here on
-      e = tables[(int64_t)b * a.max_blocks + j];
-      len = a.seq_lens[b];  // issued with the table read: one latency, not two
+      const int32_t* tb = tables + (int64_t)b * a.max_blocks;
+      const int t = table_base(b) + j;  // table index from here on
+      e = tb[t];
+      // the other warps' blocks between this warp's previous item and this one
+      for (int u = 1; u < istride; u++)
+        if (j >= u) wneg |= tb[t - u] < 0;
+      len = a.seq_lens[b];  // issued with the table reads: one latency, not two
       if constexpr (PARTIAL) beg = a.tok_begin ? a.tok_begin[b] : 0;
+      j = t;
     }
-    const unsigned negm = __ballot_sync(0xffffffffu, ok && e < 0);
+    const unsigned negm = __ballot_sync(0xffffffffu, ok && (e < 0 || wneg));
     const int prev = __shfl_up_sync(0xffffffffu, seg, 1);
     const unsigned startm = __ballot_sync(0xffffffffu, lane == 0 || seg != prev);
     const unsigned upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
@@ -416,15 +584,15 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
         y = (int)(((int64_t)e * Hkv + kvh) * BS);
       }
     }
-    const int last = min(31, nwork - 1 - base);
+    const int last = min(31, nwork - 1 - cbase);
     carry_seg = __shfl_sync(0xffffffffu, seg, last);
     carry_trunc = __shfl_sync(0xffffffffu, trunc ? 1 : 0, last);
-    ch_base = base;
+    ch_base = cbase;
     ch_y = y;
     ch_nv = nv;
   };
-  // Issue the loads of block i of this warp's range into its ring slot (all
-  // lanes call; lane 0 issues).
+  // Issue the loads of item i of this warp into its ring slot (all lanes
+  // call; lane 0 issues).
   auto produce = [&](int i) {
     if (i >= ch_base + 32) build_chunk(i & ~31);
     const int src = i - ch_base;
@@ -448,15 +616,18 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     }
   };
 
+  if (nwork > 0) build_chunk(0);  // the first 32 items' table entries
+  griddep_wait();  // K/V, q and the outputs belong to the stream order from here on
   {
     const int pre = min(nwork, STAGES);
     for (int k = 0; k < pre; k++) produce(k);
   }
   __syncwarp();
+  if (!active) return;  // a per-warp split's idle warp (no CTA barriers in that split)
 
   // ---------------- consumer state (all lanes) ----------------
-  int cb, ckvh, cj;
-  locate(f0, cb, ckvh, cj);
+  int cb, ckvh, cj_;
+  locate(u0, cb, ckvh, cj_);
   const int quad = lane >> 2;   // 0..7 : token row (S), head column (B operand)
   const int qid = lane & 3;     // 0..3
   const int mat = lane >> 3, mrow = lane & 7;
@@ -472,199 +643,210 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   // block needs neither the max reduction nor the O rescale.
   constexpr float kLazy = 8.f;
   bool timed_out = false;
+  int i_fail = 0;  // first item not consumed after a timed-out wait
+  const int G = a.G;
 
-  // q of the warp's next segment, loaded while the current one streams
+  // q of the next segment, loaded while the current one streams
   uint32_t qn[8][2];
   int qn_seg = -1;
+  const bool hv = quad < G;
+  auto load_q = [&](int qb, int qh0, uint32_t (&dst)[8][2]) {
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        a.q + ((int64_t)qb * a.H + qh0 + (hv ? quad : 0)) * D);
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+      dst[ks][0] = hv ? __ldg(qrow + ks * 8 + qid) : 0u;
+      dst[ks][1] = hv ? __ldg(qrow + ks * 8 + 4 + qid) : 0u;
+    }
+  };
 
-  int i = 0;
-  while (i < nwork && !timed_out) {
-    // ----- segment (cb, ckvh) starting at block cj
+  // Segments of the unit's range, in order. In the CTA split every warp of
+  // the CTA visits each of them (the combine's CTA barriers need it), whether
+  // or not the warp has items there.
+  int i = 0;  // next item of this warp
+  for (;;) {
     const int nb = prefix[cb + 1] - prefix[cb];
-    const int seg_j0 = cj;
-    const int64_t seg_S = (int64_t)prefix[cb] * Hkv + (int64_t)ckvh * nb;
-    const int64_t seg_E = seg_S + nb;
-    const int64_t seg_rem = f1 - seg_S;
-    const int seg_jend = seg_rem < (int64_t)nb ? (int)seg_rem : nb;
-    const int G = a.G;
+    const int seg_S = prefix[cb] * Hkv + ckvh * nb;
+    const int seg_E = seg_S + nb;
+    const int hi = min(seg_E, u1);
+    const int k_end = min(nwork, (hi - u0 - ioff + istride - 1) / istride);
     const int head0 = ckvh * G;
+    const bool whole = seg_S >= u0 && seg_E <= u1;
+    const int e_slot = (seg_S <= u0 && u0 < seg_E) ? 0 : 1;  // the range's first or last segment
 
-    // q fragments (B operand of S^T = K q^T): head n = quad, d pairs
-    const bool hv = quad < G;
-    auto load_q = [&](int qb, int qh0, uint32_t (&dst)[8][2]) {
-      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-          a.q + ((int64_t)qb * a.H + qh0 + (hv ? quad : 0)) * D);
-#pragma unroll
-      for (int ks = 0; ks < 8; ks++) {
-        dst[ks][0] = hv ? __ldg(qrow + ks * 8 + qid) : 0u;
-        dst[ks][1] = hv ? __ldg(qrow + ks * 8 + 4 + qid) : 0u;
-      }
-    };
-    uint32_t qf[8][2];
-    if (qn_seg == cb * Hkv + ckvh) {
-#pragma unroll
-      for (int ks = 0; ks < 8; ks++) { qf[ks][0] = qn[ks][0]; qf[ks][1] = qn[ks][1]; }
-    } else {
-      load_q(cb, head0, qf);
-    }
-    qn_seg = -1;
-    if (seg_E < f1) {  // the range continues into the next non-empty segment
-      int nbq = cb, nkq = ckvh + 1;
-      if (nkq == Hkv) {
-        nkq = 0;
-        do { nbq++; } while (nbq < B && prefix[nbq + 1] == prefix[nbq]);
-      }
-      if (nbq < B) {
-        load_q(nbq, nkq * G, qn);
-        qn_seg = nbq * Hkv + nkq;
-      }
-    }
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float tm0 = -INFINITY, tm1 = -INFINITY;  // true maxima (partial form)
     float o[8][4];
 #pragma unroll
     for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
 
-    // Two 16-token blocks per step: their K/V tiles feed interleaved MMA
-    // chains and share one softmax / rescale decision. A step whose second
-    // block is missing (odd count) or skipped reads the valid block's tile for
-    // both with the missing one fully masked, so no unloaded tile is read.
-    for (int j = seg_j0; j < seg_jend;) {
-      const bool two = j + 1 < seg_jend;
-      const int slotA = i % STAGES;
-      if (!mbar_wait_warp(smem_u32(&wbars[slotA]), (uint32_t)((i / STAGES) & 1), a.status)) {
-        timed_out = true;
-        break;
+    if (i < k_end) {
+      uint32_t qf[8][2];
+      if (qn_seg == cb * Hkv + ckvh) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) { qf[ks][0] = qn[ks][0]; qf[ks][1] = qn[ks][1]; }
+      } else {
+        load_q(cb, head0, qf);
       }
-      int slotB = slotA, nvB = 0, loB = 0;
-      const int infoA = winfo[slotA];
-      const int nvA = infoA & 0xff, loA = PARTIAL ? (infoA >> 8) : 0;
-      if (two) {
-        slotB = (i + 1) % STAGES;
-        if (!mbar_wait_warp(smem_u32(&wbars[slotB]), (uint32_t)(((i + 1) / STAGES) & 1), a.status)) {
+      qn_seg = -1;
+      if (k_end < nwork) {  // this warp's items continue into the next non-empty segment
+        int nbq = cb, nkq = ckvh + 1;
+        if (nkq == Hkv) {
+          nkq = 0;
+          do { nbq++; } while (nbq < B && prefix[nbq + 1] == prefix[nbq]);
+        }
+        if (nbq < B) {
+          load_q(nbq, nkq * G, qn);
+          qn_seg = nbq * Hkv + nkq;
+        }
+      }
+
+      // Two items per step: their K/V tiles feed interleaved MMA chains and
+      // share one softmax / rescale decision. A step whose second item is
+      // missing (odd count) or skipped reads the valid block's tile for both
+      // with the missing one fully masked, so no unloaded tile is read.
+      while (i < k_end) {
+        const bool two = i + 1 < k_end;
+        const int step = two ? 2 : 1;
+        if (timed_out) {  // keep the visiting order; no more loads or math
+          i += step;
+          continue;
+        }
+        const int slotA = i % STAGES;
+        if (!mbar_wait_warp(smem_u32(&wbars[slotA]), (uint32_t)((i / STAGES) & 1), a.status)) {
           timed_out = true;
-          break;
+          i_fail = i;
+          continue;
         }
-        const int infoB = winfo[slotB];
-        nvB = infoB & 0xff;
-        if constexpr (PARTIAL) loB = infoB >> 8;
-      }
-      if (nvA > 0 || nvB > 0) {
-        uint32_t kA = ring + slotA * STAGE, kB = ring + slotB * STAGE;
-        if (nvA == 0) kA = kB;
-        if (nvB == 0) kB = kA;
-        // zero V rows outside the valid tokens so 0 * garbage cannot be NaN
-        if (nvA > 0 && nvA < BS) {
-          uint8_t* vt = base + (kA + TILE - base_u32);
-          for (int x = lane; x < (BS - nvA) * 16; x += 32) {
-            const int r = nvA + (x >> 4), c = x & 15;
-            *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
+        int slotB = slotA, nvB = 0, loB = 0;
+        const int infoA = winfo[slotA];
+        const int nvA = infoA & 0xff, loA = PARTIAL ? (infoA >> 8) : 0;
+        if (two) {
+          slotB = (i + 1) % STAGES;
+          if (!mbar_wait_warp(smem_u32(&wbars[slotB]), (uint32_t)(((i + 1) / STAGES) & 1), a.status)) {
+            timed_out = true;
+            i_fail = i;
+            continue;
           }
+          const int infoB = winfo[slotB];
+          nvB = infoB & 0xff;
+          if constexpr (PARTIAL) loB = infoB >> 8;
         }
-        if (nvB > 0 && nvB < BS) {
-          uint8_t* vt = base + (kB + TILE - base_u32);
-          for (int x = lane; x < (BS - nvB) * 16; x += 32) {
-            const int r = nvB + (x >> 4), c = x & 15;
-            *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
-          }
-        }
-        if constexpr (PARTIAL) {  // rows before the range start
-          if (nvA > 0 && loA > 0) {
+        if (nvA > 0 || nvB > 0) {
+          uint32_t kA = ring + slotA * STAGE, kB = ring + slotB * STAGE;
+          if (nvA == 0) kA = kB;
+          if (nvB == 0) kB = kA;
+          // zero V rows outside the valid tokens so 0 * garbage cannot be NaN
+          if (nvA > 0 && nvA < BS) {
             uint8_t* vt = base + (kA + TILE - base_u32);
-            for (int x = lane; x < loA * 16; x += 32)
-              *reinterpret_cast<uint4*>(vt + tile_off(x >> 4, x & 15)) = make_uint4(0, 0, 0, 0);
+            for (int x = lane; x < (BS - nvA) * 16; x += 32) {
+              const int r = nvA + (x >> 4), c = x & 15;
+              *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
+            }
           }
-          if (nvB > 0 && loB > 0) {
+          if (nvB > 0 && nvB < BS) {
             uint8_t* vt = base + (kB + TILE - base_u32);
-            for (int x = lane; x < loB * 16; x += 32)
-              *reinterpret_cast<uint4*>(vt + tile_off(x >> 4, x & 15)) = make_uint4(0, 0, 0, 0);
+            for (int x = lane; x < (BS - nvB) * 16; x += 32) {
+              const int r = nvB + (x >> 4), c = x & 15;
+              *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          if constexpr (PARTIAL) {  // rows before the range start
+            if (nvA > 0 && loA > 0) {
+              uint8_t* vt = base + (kA + TILE - base_u32);
+              for (int x = lane; x < loA * 16; x += 32)
+                *reinterpret_cast<uint4*>(vt + tile_off(x >> 4, x & 15)) = make_uint4(0, 0, 0, 0);
+            }
+            if (nvB > 0 && loB > 0) {
+              uint8_t* vt = base + (kB + TILE - base_u32);
+              for (int x = lane; x < loB * 16; x += 32)
+                *reinterpret_cast<uint4*>(vt + tile_off(x >> 4, x & 15)) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          __syncwarp();
+          // S^T = K q^T for both blocks, four independent chains
+          float sA[4] = {0.f, 0.f, 0.f, 0.f}, sA2[4] = {0.f, 0.f, 0.f, 0.f};
+          float sB[4] = {0.f, 0.f, 0.f, 0.f}, sB2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < 8; ks += 2) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0_, c1_, c2_, c3_, d0, d1, d2, d3;
+            ldsm_x4(kA + kofs[ks], a0, a1, a2, a3);
+            ldsm_x4(kB + kofs[ks], b0, b1, b2, b3);
+            ldsm_x4(kA + kofs[ks + 1], c0_, c1_, c2_, c3_);
+            ldsm_x4(kB + kofs[ks + 1], d0, d1, d2, d3);
+            mma_bf16_16816(sA, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            mma_bf16_16816(sB, b0, b1, b2, b3, qf[ks][0], qf[ks][1]);
+            mma_bf16_16816(sA2, c0_, c1_, c2_, c3_, qf[ks + 1][0], qf[ks + 1][1]);
+            mma_bf16_16816(sB2, d0, d1, d2, d3, qf[ks + 1][0], qf[ks + 1][1]);
+          }
+          // mask + scale to log2 units
+          const float sc = a.scale_log2;
+          const bool va0 = quad < nvA && quad >= loA, va1 = quad + 8 < nvA && quad + 8 >= loA;
+          const bool vb0 = quad < nvB && quad >= loB, vb1 = quad + 8 < nvB && quad + 8 >= loB;
+          sA[0] = va0 ? (sA[0] + sA2[0]) * sc : -INFINITY;
+          sA[1] = va0 ? (sA[1] + sA2[1]) * sc : -INFINITY;
+          sA[2] = va1 ? (sA[2] + sA2[2]) * sc : -INFINITY;
+          sA[3] = va1 ? (sA[3] + sA2[3]) * sc : -INFINITY;
+          sB[0] = vb0 ? (sB[0] + sB2[0]) * sc : -INFINITY;
+          sB[1] = vb0 ? (sB[1] + sB2[1]) * sc : -INFINITY;
+          sB[2] = vb1 ? (sB[2] + sB2[2]) * sc : -INFINITY;
+          sB[3] = vb1 ? (sB[3] + sB2[3]) * sc : -INFINITY;
+          const float c0m = fmaxf(fmaxf(sA[0], sA[2]), fmaxf(sB[0], sB[2]));
+          const float c1m = fmaxf(fmaxf(sA[1], sA[3]), fmaxf(sB[1], sB[3]));
+          if constexpr (PARTIAL) { tm0 = fmaxf(tm0, c0m); tm1 = fmaxf(tm1, c1m); }
+          const bool grow = c0m > m0 + kLazy || c1m > m1 + kLazy;
+          if (__any_sync(0xffffffffu, grow)) {
+            float bm0 = c0m, bm1 = c1m;
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+              bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+              bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+            }
+            const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+            const float al0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mn0);
+            const float al1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mn1);
+            m0 = mn0; m1 = mn1;
+            l0 *= al0; l1 *= al1;
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+              o[t][0] *= al0; o[t][1] *= al1; o[t][2] *= al0; o[t][3] *= al1;
+            }
+          }
+          float pA[4], pB[4];
+#pragma unroll
+          for (int r = 0; r < 4; r++) {
+            const float mr = (r & 1) ? m1 : m0;
+            pA[r] = sA[r] == -INFINITY ? 0.f : ex2(sA[r] - mr);
+            pB[r] = sB[r] == -INFINITY ? 0.f : ex2(sB[r] - mr);
+          }
+          l0 += (pA[0] + pA[2]) + (pB[0] + pB[2]);
+          l1 += (pA[1] + pA[3]) + (pB[1] + pB[3]);
+          // P^T as the B operand: transpose the (tok x head) halves
+          const uint32_t ba0 = movm_t(pack_bf16x2(pA[0], pA[1]));
+          const uint32_t ba1 = movm_t(pack_bf16x2(pA[2], pA[3]));
+          const uint32_t bb0 = movm_t(pack_bf16x2(pB[0], pB[1]));
+          const uint32_t bb1 = movm_t(pack_bf16x2(pB[2], pB[3]));
+          // O^T[128 d][8 heads] += V_A^T P_A^T + V_B^T P_B^T
+          const uint32_t vA = kA + TILE, vB = kB + TILE;
+#pragma unroll
+          for (int t = 0; t < 8; t++) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            ldsm_x4_t(vA + vofs[t], a0, a1, a2, a3);
+            ldsm_x4_t(vB + vofs[t], b0, b1, b2, b3);
+            mma_bf16_16816(o[t], a0, a1, a2, a3, ba0, ba1);
+            mma_bf16_16816(o[t], b0, b1, b2, b3, bb0, bb1);
           }
         }
         __syncwarp();
-        // S^T = K q^T for both blocks, four independent chains
-        float sA[4] = {0.f, 0.f, 0.f, 0.f}, sA2[4] = {0.f, 0.f, 0.f, 0.f};
-        float sB[4] = {0.f, 0.f, 0.f, 0.f}, sB2[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < 8; ks += 2) {
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3, d0, d1, d2, d3;
-          ldsm_x4(kA + kofs[ks], a0, a1, a2, a3);
-          ldsm_x4(kB + kofs[ks], b0, b1, b2, b3);
-          ldsm_x4(kA + kofs[ks + 1], c0, c1, c2, c3);
-          ldsm_x4(kB + kofs[ks + 1], d0, d1, d2, d3);
-          mma_bf16_16816(sA, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
-          mma_bf16_16816(sB, b0, b1, b2, b3, qf[ks][0], qf[ks][1]);
-          mma_bf16_16816(sA2, c0, c1, c2, c3, qf[ks + 1][0], qf[ks + 1][1]);
-          mma_bf16_16816(sB2, d0, d1, d2, d3, qf[ks + 1][0], qf[ks + 1][1]);
-        }
-        // mask + scale to log2 units
-        const float sc = a.scale_log2;
-        const bool va0 = quad < nvA && quad >= loA, va1 = quad + 8 < nvA && quad + 8 >= loA;
-        const bool vb0 = quad < nvB && quad >= loB, vb1 = quad + 8 < nvB && quad + 8 >= loB;
-        sA[0] = va0 ? (sA[0] + sA2[0]) * sc : -INFINITY;
-        sA[1] = va0 ? (sA[1] + sA2[1]) * sc : -INFINITY;
-        sA[2] = va1 ? (sA[2] + sA2[2]) * sc : -INFINITY;
-        sA[3] = va1 ? (sA[3] + sA2[3]) * sc : -INFINITY;
-        sB[0] = vb0 ? (sB[0] + sB2[0]) * sc : -INFINITY;
-        sB[1] = vb0 ? (sB[1] + sB2[1]) * sc : -INFINITY;
-        sB[2] = vb1 ? (sB[2] + sB2[2]) * sc : -INFINITY;
-        sB[3] = vb1 ? (sB[3] + sB2[3]) * sc : -INFINITY;
-        const float c0m = fmaxf(fmaxf(sA[0], sA[2]), fmaxf(sB[0], sB[2]));
-        const float c1m = fmaxf(fmaxf(sA[1], sA[3]), fmaxf(sB[1], sB[3]));
-        if constexpr (PARTIAL) { tm0 = fmaxf(tm0, c0m); tm1 = fmaxf(tm1, c1m); }
-        const bool grow = c0m > m0 + kLazy || c1m > m1 + kLazy;
-        if (__any_sync(0xffffffffu, grow)) {
-          float bm0 = c0m, bm1 = c1m;
-#pragma unroll
-          for (int off = 4; off < 32; off <<= 1) {
-            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
-            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
-          }
-          const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
-          const float al0 = (m0 == -INFINITY) ? 0.f : ex2(m0 - mn0);
-          const float al1 = (m1 == -INFINITY) ? 0.f : ex2(m1 - mn1);
-          m0 = mn0; m1 = mn1;
-          l0 *= al0; l1 *= al1;
-#pragma unroll
-          for (int t = 0; t < 8; t++) {
-            o[t][0] *= al0; o[t][1] *= al1; o[t][2] *= al0; o[t][3] *= al1;
-          }
-        }
-        float pA[4], pB[4];
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-          const float mr = (r & 1) ? m1 : m0;
-          pA[r] = sA[r] == -INFINITY ? 0.f : ex2(sA[r] - mr);
-          pB[r] = sB[r] == -INFINITY ? 0.f : ex2(sB[r] - mr);
-        }
-        l0 += (pA[0] + pA[2]) + (pB[0] + pB[2]);
-        l1 += (pA[1] + pA[3]) + (pB[1] + pB[3]);
-        // P^T as the B operand: transpose the (tok x head) halves
-        const uint32_t ba0 = movm_t(pack_bf16x2(pA[0], pA[1]));
-        const uint32_t ba1 = movm_t(pack_bf16x2(pA[2], pA[3]));
-        const uint32_t bb0 = movm_t(pack_bf16x2(pB[0], pB[1]));
-        const uint32_t bb1 = movm_t(pack_bf16x2(pB[2], pB[3]));
-        // O^T[128 d][8 heads] += V_A^T P_A^T + V_B^T P_B^T
-        const uint32_t vA = kA + TILE, vB = kB + TILE;
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          ldsm_x4_t(vA + vofs[t], a0, a1, a2, a3);
-          ldsm_x4_t(vB + vofs[t], b0, b1, b2, b3);
-          mma_bf16_16816(o[t], a0, a1, a2, a3, ba0, ba1);
-          mma_bf16_16816(o[t], b0, b1, b2, b3, bb0, bb1);
-        }
+        if (i + STAGES < nwork) produce(i + STAGES);
+        if (two && i + 1 + STAGES < nwork) produce(i + 1 + STAGES);
+        __syncwarp();
+        i += step;
       }
-      __syncwarp();
-      if (i + STAGES < nwork) produce(i + STAGES);
-      if (two && i + 1 + STAGES < nwork) produce(i + 1 + STAGES);
-      __syncwarp();
-      const int step = two ? 2 : 1;
-      i += step;
-      j += step;
     }
-    if (timed_out) break;
 
-    // ----- finish the segment
+
+    // ----- finish the segment: this warp's share (natural-log m)
     float L0 = l0, L1 = l1;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
@@ -672,7 +854,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       L1 += __shfl_xor_sync(0xffffffffu, L1, off);
     }
     const int n0 = 2 * qid, n1 = 2 * qid + 1;  // head columns of this lane
-    float mo0 = m0 * LN2, mo1 = m1 * LN2;      // reference maxima, natural-log units
+    float mo0 = m0 * LN2, mo1 = m1 * LN2;
     if constexpr (PARTIAL) {
       // Re-base (l, o) from the lazily moved running max to the true maximum
       // of the range, so that m is the maximum score as the triple promises.
@@ -688,162 +870,124 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
       for (int t = 0; t < 8; t++) { o[t][0] *= f0; o[t][2] *= f0; o[t][1] *= f1; o[t][3] *= f1; }
       mo0 = tm0 * LN2; mo1 = tm1 * LN2;
     }
-    const bool whole = (seg_S >= f0) && (seg_E <= f1);
-    if (whole && PARTIAL) {
-      const int64_t row = (int64_t)cb * a.H + head0;
-      if (quad == 0) {
-        if (n0 < G) { a.m_out[row + n0] = mo0; a.l_out[row + n0] = L0; }
-        if (n1 < G) { a.m_out[row + n1] = mo1; a.l_out[row + n1] = L1; }
-      }
-      float* ob = a.o_out + row * D;
-#pragma unroll
-      for (int t = 0; t < 8; t++) {
-        const int d0 = 16 * t + quad;
-        if (n0 < G) { ob[n0 * D + d0] = o[t][0]; ob[n0 * D + d0 + 8] = o[t][2]; }
-        if (n1 < G) { ob[n1 * D + d0] = o[t][1]; ob[n1 * D + d0 + 8] = o[t][3]; }
-      }
-    } else if (whole) {
-      const float i0 = L0 > 0.f ? 1.f / L0 : 0.f, i1 = L1 > 0.f ? 1.f / L1 : 0.f;
-      __nv_bfloat16* ob = a.out + ((int64_t)cb * a.H + head0) * D;
-#pragma unroll
-      for (int t = 0; t < 8; t++) {
-        const int d0 = 16 * t + quad;
-        if (n0 < G) {
-          ob[n0 * D + d0] = __float2bfloat16_rn(o[t][0] * i0);
-          ob[n0 * D + d0 + 8] = __float2bfloat16_rn(o[t][2] * i0);
+    if (L0 == 0.f) mo0 = -INFINITY;  // no valid token: an empty partial
+    if (L1 == 0.f) mo1 = -INFINITY;
+    const int cidx = 2 + cb * Hkv + ckvh;  // this segment's merge counter
+    const int ca = owner_unit(seg_S, uper, urem), cz = owner_unit(seg_E - 1, uper, urem);
+    const int nc = cz - ca + 1;
+    // slot of contributor ca + k: its range's first segment (0) or last (1)
+    auto slot_of = [&](int k) -> const Partial* {
+      return a.partials + 2 * (ca + k) + ((k == 0 && unit_start(ca, uper, urem) < seg_S) ? 1 : 0);
+    };
+
+    if (!grouped) {
+      // ---- per-warp split: the segment's blocks of this range are all in registers
+      if (whole && PARTIAL) {
+        const int64_t row = (int64_t)cb * a.H + head0;
+        if (quad == 0) {
+          if (n0 < G) { a.m_out[row + n0] = mo0; a.l_out[row + n0] = L0; }
+          if (n1 < G) { a.m_out[row + n1] = mo1; a.l_out[row + n1] = L1; }
         }
-        if (n1 < G) {
-          ob[n1 * D + d0] = __float2bfloat16_rn(o[t][1] * i1);
-          ob[n1 * D + d0 + 8] = __float2bfloat16_rn(o[t][3] * i1);
+        float* ob = a.o_out + row * D;
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+          const int d0 = 16 * t + quad;
+          if (n0 < G) { ob[n0 * D + d0] = o[t][0]; ob[n0 * D + d0 + 8] = o[t][2]; }
+          if (n1 < G) { ob[n1 * D + d0] = o[t][1]; ob[n1 * D + d0 + 8] = o[t][3]; }
+        }
+      } else if (whole) {
+        const float i0 = L0 > 0.f ? 1.f / L0 : 0.f, i1 = L1 > 0.f ? 1.f / L1 : 0.f;
+        __nv_bfloat16* ob = a.out + ((int64_t)cb * a.H + head0) * D;
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+          const int d0 = 16 * t + quad;
+          if (n0 < G) {
+            ob[n0 * D + d0] = __float2bfloat16_rn(o[t][0] * i0);
+            ob[n0 * D + d0 + 8] = __float2bfloat16_rn(o[t][2] * i0);
+          }
+          if (n1 < G) {
+            ob[n1 * D + d0] = __float2bfloat16_rn(o[t][1] * i1);
+            ob[n1 * D + d0 + 8] = __float2bfloat16_rn(o[t][3] * i1);
+          }
+        }
+      } else {
+        Partial* pp = a.partials + 2 * unit + e_slot;
+        if (quad == 0) {
+          if (n0 < G) { pp->m[n0] = mo0; pp->l[n0] = L0; }
+          if (n1 < G) { pp->m[n1] = mo1; pp->l[n1] = L1; }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+          const int d0 = 16 * t + quad;
+          if (n0 < G) { pp->o[n0][d0] = o[t][0]; pp->o[n0][d0 + 8] = o[t][2]; }
+          if (n1 < G) { pp->o[n1][d0] = o[t][1]; pp->o[n1][d0 + 8] = o[t][3]; }
+        }
+        __threadfence();  // the partial before the count
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&a.counters[cidx], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == nc - 1) {  // the last contributor merges
+          __threadfence();
+          merge_units_all<PARTIAL>(a, (int64_t)cb * a.H + head0, G, nc, lane, slot_of);
+          if (lane == 0) a.counters[cidx] = 0;
         }
       }
     } else {
-      const int e = (seg_S <= f0 && f0 < seg_E) ? 0 : 1;
-      Partial* pp = a.partials + 2 * gw + e;
+      // ---- CTA split: stage the warps' shares, combine them (warp w: heads w, w + WARPS, ...)
+      WarpPart& wp = wpart[warp];
       if (quad == 0) {
-        if (n0 < G) { pp->m[n0] = mo0; pp->l[n0] = L0; }
-        if (n1 < G) { pp->m[n1] = mo1; pp->l[n1] = L1; }
+        if (n0 < G) { wp.m[n0] = mo0; wp.l[n0] = L0; }
+        if (n1 < G) { wp.m[n1] = mo1; wp.l[n1] = L1; }
       }
+      if (L0 > 0.f || L1 > 0.f) {
 #pragma unroll
-      for (int t = 0; t < 8; t++) {
-        const int d0 = 16 * t + quad;
-        if (n0 < G) { pp->o[n0][d0] = o[t][0]; pp->o[n0][d0 + 8] = o[t][2]; }
-        if (n1 < G) { pp->o[n1][d0] = o[t][1]; pp->o[n1][d0 + 8] = o[t][3]; }
+        for (int t = 0; t < 8; t++) {
+          const int d0 = 16 * t + quad;
+          if (n0 < G) { wp.o[n0][d0] = o[t][0]; wp.o[n0][d0 + 8] = o[t][2]; }
+          if (n1 < G) { wp.o[n1][d0] = o[t][1]; wp.o[n1][d0 + 8] = o[t][3]; }
+        }
       }
-      if (!barrier_mode) {
-      __threadfence();
-      __syncwarp();
-      const int cidx = 2 + cb * Hkv + ckvh;  // [0..1]: grid barrier words
-      const int wa = owner_warp(seg_S, TB, W), wb = owner_warp(seg_E - 1, TB, W);
-      const int ncontrib = wb - wa + 1;
-      int old = 0;
-      if (lane == 0) old = atomicAdd(&a.counters[cidx], 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == ncontrib - 1) {
-        __threadfence();
-        // merge all contributors of this (sequence, kv head); lanes work on
-        // different contributors so the L2 reads overlap (long contexts split
-        // one sequence over dozens of warps)
-        const int nc = ncontrib;
-        auto slot_of = [&](int c) -> const Partial* {
-          const int64_t fc = (int64_t)c * TB / W;
-          return a.partials + 2 * c + ((c == wa && fc < seg_S) ? 1 : 0);
-        };
-        // Lane c holds contributor c's (m, l) for every head; the rows of
-        // contributors 0 and 1 are loaded in the same round, so a split of
-        // up to two contributors costs one L2 round trip before the math.
-        float M[MAX_G], den[MAX_G], mc[MAX_G], lc[MAX_G];
-        float4 x1[MAX_G], x2[MAX_G];
-        {
-          const bool mine = lane < nc;
-          const Partial* pc = slot_of(wa + (mine ? lane : 0));
-          const float4* o1 = reinterpret_cast<const float4*>(&slot_of(wa)->o[0][0]) + lane;
-          const float4* o2 = reinterpret_cast<const float4*>(&slot_of(wa + (nc > 1 ? 1 : 0))->o[0][0]) + lane;
+      cta_bar<WARPS>();
+      Partial* cpart = a.partials + 2 * unit + e_slot;
+      for (int n = warp; n < G; n += WARPS) {
+        float mw[WARPS], M = -INFINITY;
 #pragma unroll
-          for (int n = 0; n < MAX_G; n++) {
-            mc[n] = -INFINITY;
-            lc[n] = 0.f;
-            if (n < G) {
-              if (mine) { mc[n] = __ldcg(&pc->m[n]); lc[n] = __ldcg(&pc->l[n]); }
-              x1[n] = __ldcg(o1 + n * (D / 4));
-              x2[n] = __ldcg(o2 + n * (D / 4));
-            }
-          }
+        for (int w = 0; w < WARPS; w++) { mw[w] = wpart[w].m[n]; M = fmaxf(M, mw[w]); }
+        float den = 0.f;
+        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < WARPS; w++) {
+          if (mw[w] == -INFINITY) continue;  // uniform over the warp
+          const float wt = __expf(mw[w] - M);
+          den += wt * wpart[w].l[n];
+          const float4 x = reinterpret_cast<const float4*>(wpart[w].o[n])[lane];
+          num.x += wt * x.x; num.y += wt * x.y; num.z += wt * x.z; num.w += wt * x.w;
         }
-#pragma unroll
-        for (int n = 0; n < MAX_G; n++) { M[n] = mc[n]; den[n] = 0.f; }
-        // contributors past 32 (very long sequences): their maxima too
-        for (int c0 = 32; c0 < nc; c0 += 32)
-          if (c0 + lane < nc) {
-            const Partial* pc = slot_of(wa + c0 + lane);
-#pragma unroll
-            for (int n = 0; n < MAX_G; n++)
-              if (n < G) M[n] = fmaxf(M[n], __ldcg(&pc->m[n]));
-          }
-#pragma unroll
-        for (int n = 0; n < MAX_G; n++)
-#pragma unroll
-          for (int off = 16; off; off >>= 1) M[n] = fmaxf(M[n], __shfl_xor_sync(0xffffffffu, M[n], off));
-        float4 num[MAX_G];
-#pragma unroll
-        for (int n = 0; n < MAX_G; n++) num[n] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c0 = 0; c0 < nc; c0 += 32) {
-          float wl[MAX_G];
-          if (c0 + lane < nc) {
-            const Partial* pc = slot_of(wa + c0 + lane);
-#pragma unroll
-            for (int n = 0; n < MAX_G; n++) {
-              wl[n] = 0.f;
-              if (n < G) {
-                const float m_ = c0 == 0 ? mc[n] : __ldcg(&pc->m[n]);
-                const float l_ = c0 == 0 ? lc[n] : __ldcg(&pc->l[n]);
-                wl[n] = (m_ == -INFINITY) ? 0.f : __expf(m_ - M[n]);
-                den[n] += wl[n] * l_;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int n = 0; n < MAX_G; n++) wl[n] = 0.f;
-          }
-          const int cnt = min(32, nc - c0);
-          for (int k = 0; k < cnt; k += 2) {
-            const bool second = k + 1 < cnt;
-            if (c0 + k > 0) {  // rows of contributors 0 and 1 are already loaded
-              const float4* o1 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k)->o[0][0]) + lane;
-              const float4* o2 = reinterpret_cast<const float4*>(&slot_of(wa + c0 + k + (second ? 1 : 0))->o[0][0]) + lane;
-#pragma unroll
-              for (int n = 0; n < MAX_G; n++) {
-                if (n < G) {
-                  x1[n] = __ldcg(o1 + n * (D / 4));
-                  x2[n] = __ldcg(o2 + n * (D / 4));
-                }
-              }
-            }
-#pragma unroll
-            for (int n = 0; n < MAX_G; n++) {
-              const float w1 = __shfl_sync(0xffffffffu, wl[n], k);
-              const float w2 = second ? __shfl_sync(0xffffffffu, wl[n], k + 1) : 0.f;
-              if (n < G) {
-                num[n].x += w1 * x1[n].x + w2 * x2[n].x;
-                num[n].y += w1 * x1[n].y + w2 * x2[n].y;
-                num[n].z += w1 * x1[n].z + w2 * x2[n].z;
-                num[n].w += w1 * x1[n].w + w2 * x2[n].w;
-              }
-            }
-          }
+        if (whole) {
+          emit_merged<PARTIAL>(a, (int64_t)cb * a.H + head0 + n, lane, M, den, num);
+        } else {
+          if (lane == 0) { cpart->m[n] = M; cpart->l[n] = den; }
+          reinterpret_cast<float4*>(cpart->o[n])[lane] = num;
         }
-#pragma unroll
-        for (int n = 0; n < MAX_G; n++) {
-#pragma unroll
-          for (int off = 16; off; off >>= 1) den[n] += __shfl_xor_sync(0xffffffffu, den[n], off);
-          if (n < G) emit_merged<PARTIAL>(a, (int64_t)cb * a.H + head0 + n, lane, M[n], den[n], num[n]);
-        }
-        if (lane == 0) a.counters[cidx] = 0;
       }
-      }  // !barrier_mode
+      if (!whole) __threadfence();  // this CTA's partial before its count
+      cta_bar<WARPS>();             // the staged shares may be overwritten from here on
+      if (!whole) {
+        // the last CTA to finish a split segment merges the CTAs' partials
+        if (tid == 0) s_last = atomicAdd(&a.counters[cidx], 1) == nc - 1;
+        cta_bar<WARPS>();
+        if (s_last) {
+          __threadfence();
+          for (int n = warp; n < G; n += WARPS)
+            merge_units<PARTIAL>(a, (int64_t)cb * a.H + head0 + n, n, nc, lane, slot_of);
+          if (tid == 0) a.counters[cidx] = 0;
+        }
+      }
     }
-    // advance consumer to the next segment
-    cj = 0;
+
+    // advance to the next non-empty segment of the unit's range
+    if (seg_E >= u1) break;
     if (++ckvh == Hkv) {
       ckvh = 0;
       do { cb++; } while (cb < B && prefix[cb + 1] == prefix[cb]);
@@ -852,68 +996,9 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
 
   if (timed_out) {
     // Drain the loads this warp still has in flight (bounded) before exit.
-    for (int k = i + 1; k < min(nwork, i + STAGES); k++) {
+    for (int k = i_fail; k < min(nwork, i_fail + STAGES); k++) {
       const int slot = k % STAGES;
       if (!mbar_wait_warp(smem_u32(&wbars[slot]), (uint32_t)((k / STAGES) & 1), a.status)) break;
-    }
-  }
-  }  // nwork > 0
-
-  // ---- every partial triple is written: merge the split (sequence, kv head)
-  // pairs. Head n of a pair is merged by its contributor warp (n mod count),
-  // so the merges of long sequences spread over many warps.
-  if (!barrier_mode) return;
-  if (!grid_barrier(a.counters, a.status) || nwork <= 0) return;
-  auto slot_of = [&](int c, int wa, int64_t S) -> const Partial* {
-    const int64_t fc = (int64_t)c * TB / W;
-    return a.partials + 2 * c + ((c == wa && fc < S) ? 1 : 0);
-  };
-  for (int pass = 0; pass < 2; pass++) {
-    int b, kvh, j;
-    locate(pass == 0 ? f0 : f1 - 1, b, kvh, j);
-    const int nb = prefix[b + 1] - prefix[b];
-    const int64_t S = (int64_t)prefix[b] * Hkv + (int64_t)kvh * nb, E = S + nb;
-    if (pass == 1 && S <= f0) break;       // the last segment is the first one
-    if (S >= f0 && E <= f1) continue;      // whole: already written
-    const int wa = owner_warp(S, TB, W), wb = owner_warp(E - 1, TB, W);
-    const int nc = wb - wa + 1;
-    const int G = a.G;
-    for (int n = gw - wa; n < G; n += nc) {
-      float M = -INFINITY;
-      for (int c0 = 0; c0 < nc; c0 += 32)
-        if (c0 + lane < nc) M = fmaxf(M, __ldcg(&slot_of(wa + c0 + lane, wa, S)->m[n]));
-#pragma unroll
-      for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-      float den = 0.f;
-      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c0 = 0; c0 < nc; c0 += 32) {
-        float wl = 0.f;
-        if (c0 + lane < nc) {
-          const Partial* pc = slot_of(wa + c0 + lane, wa, S);
-          const float mc = __ldcg(&pc->m[n]);
-          wl = (mc == -INFINITY) ? 0.f : __expf(mc - M);
-          den += wl * __ldcg(&pc->l[n]);
-        }
-        const int cnt = min(32, nc - c0);
-        for (int k0 = 0; k0 < cnt; k0 += 8) {
-          float4 x[8];
-#pragma unroll
-          for (int u = 0; u < 8; u++)  // eight rows in flight
-            x[u] = (k0 + u < cnt)
-                       ? __ldcg(reinterpret_cast<const float4*>(&slot_of(wa + c0 + k0 + u, wa, S)->o[n][0]) + lane)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int u = 0; u < 8; u++) {
-            const float w = __shfl_sync(0xffffffffu, wl, (k0 + u) & 31);
-            if (k0 + u < cnt) {
-              num.x += w * x[u].x; num.y += w * x[u].y; num.z += w * x[u].z; num.w += w * x[u].w;
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-      emit_merged<PARTIAL>(a, (int64_t)b * a.H + kvh * G + n, lane, M, den, num);
     }
   }
 }
@@ -936,7 +1021,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Warps per CTA (one CTA per SM) and ring depth per warp. Measured on B200
 // (C2 step): one consumer warp per SM sub-partition is fastest -- 4 warps
 // reach 86 % of the copy bandwidth (4, 5 or 6 stages alike), 8 warps x 3
-// stages only 72 %, 3 warps 74 %, 2 warps 52 %.
+// stages only 72 %, 3 warps 74 %, 2 warps 52 %. The partial form keeps the
+// per-sequence table offsets in shared memory too and runs 5 stages.
 #ifndef ZL_DECODE_WARPS
 #define ZL_DECODE_WARPS 4
 #endif
@@ -945,23 +1031,32 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 #endif
 constexpr int kWarps = ZL_DECODE_WARPS;
 constexpr int kStages = ZL_DECODE_STAGES;
+constexpr int kStagesPartial = kStages - 1;
+static_assert(Smem<kWarps, kStages, false>::kTotal <= 232448, "shared memory of the normalised form");
+static_assert(Smem<kWarps, kStagesPartial, true>::kTotal <= 232448, "shared memory of the partial form");
 
-// Cooperative launch: the grid (one CTA per SM) must be co-resident because its
-// CTAs meet at a grid barrier before merging split partials.
+// One CTA per SM. With pdl the launch may begin while the previous kernel on
+// the stream still runs (programmatic stream serialization); the kernel's
+// griddep_wait keeps every dependent access in stream order.
 template <typename Kern>
-cudaError_t launch_cooperative(Kern kern, int grid, int smem, cudaStream_t st, const DecodeArgs& args,
-                               const CUtensorMap& tk, const CUtensorMap& tv) {
+cudaError_t launch_decode(Kern kern, int grid, int smem, cudaStream_t st, const DecodeArgs& args,
+                          const CUtensorMap& tk, const CUtensorMap& tv, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kWarps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, args, tk, tv);
+}
+
+// Flat work items (sequence, kv head, block) are indexed in 32 bits.
+inline bool flat_index_fits(int B, int max_blocks, int Hkv) {
+  return (int64_t)B * max_blocks * Hkv < (1ll << 31);
 }
 
 }  // namespace
@@ -999,7 +1094,7 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
       map != ZL_GQA_GROUPED && H != Hkv)
     return ZL_ERR_UNSUPPORTED;
   const uint64_t rows = (uint64_t)num_blocks * Hkv * BS;
-  if (rows == 0 || rows >= (1ull << 31)) return ZL_ERR_UNSUPPORTED;
+  if (rows == 0 || rows >= (1ull << 31) || !flat_index_fits(B, max_blocks, Hkv)) return ZL_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool) |
        reinterpret_cast<uintptr_t>(partial ? (void*)o_out : out)) & 15)
     return ZL_ERR_UNSUPPORTED;
@@ -1012,8 +1107,7 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
   if (s != ZL_OK) return s;
 
   const int grid = ctx->num_sms;
-  const int64_t W = (int64_t)grid * kWarps;
-  s = ensure_workspace(ctx, sizeof(Partial) * 2 * W);
+  s = ensure_workspace(ctx, sizeof(Partial) * 2 * grid * kWarps);
   if (s != ZL_OK) return s;
   s = ensure_counters(ctx, sizeof(int) * (2 + (size_t)B * Hkv));
   if (s != ZL_OK) return s;
@@ -1033,6 +1127,7 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
   args.B = B; args.H = H; args.Hkv = Hkv; args.G = H / Hkv; args.max_blocks = max_blocks;
   args.num_blocks = num_blocks;
   args.scale_log2 = scale * LOG2E;
+  args.inputs_ahead = (ctx->flags & ZL_CTX_INPUTS_AHEAD) ? 1 : 0;
 
   // the shared-memory limit is a per-device attribute of each function
   auto set_smem = [&](auto kern, int bytes, std::atomic<uint64_t>& done) -> cudaError_t {
@@ -1044,17 +1139,17 @@ zl_status launch_decode_bf16_fast(zl_ctx* ctx, const void* q, const void* k_pool
     return cudaSuccess;
   };
   if (partial) {
-    using SM = Smem<kWarps, kStages, true>;
-    auto kern = paged_decode_bf16_kernel<kWarps, kStages, true>;
+    using SM = Smem<kWarps, kStagesPartial, true>;
+    auto kern = paged_decode_bf16_kernel<kWarps, kStagesPartial, true>;
     static std::atomic<uint64_t> attr_set{0};
     ZL_CUDA_TRY(set_smem(kern, SM::kTotal, attr_set));
-    ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
+    ZL_CUDA_TRY(launch_decode(kern, grid, SM::kTotal, st, args, tk, tv, true));
   } else {
     using SM = Smem<kWarps, kStages, false>;
     auto kern = paged_decode_bf16_kernel<kWarps, kStages, false>;
     static std::atomic<uint64_t> attr_set{0};
     ZL_CUDA_TRY(set_smem(kern, SM::kTotal, attr_set));
-    ZL_CUDA_TRY(launch_cooperative(kern, grid, SM::kTotal, st, args, tk, tv));
+    ZL_CUDA_TRY(launch_decode(kern, grid, SM::kTotal, st, args, tk, tv, true));
   }
   ZL_LAUNCH_CHECK(ctx);
   return ZL_OK;
@@ -1160,6 +1255,9 @@ extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, 
   if (rows >= (1ull << 31))
     return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: pool of %lld blocks is too large",
                      (long long)num_blocks);
+  if (!flat_index_fits(num_seqs, max_blocks_per_seq, num_kv_heads))
+    return set_error(ZL_ERR_INVALID_ARG, "paged_decode_noalloc: num_seqs x max_blocks_per_seq x num_kv_heads "
+                     "must stay below 2^31");
   if (!status)
     return set_error(ZL_ERR_INVALID_ARG,
                      "paged_decode_noalloc: a device status word is required (device-side errors "
@@ -1204,9 +1302,11 @@ extern "C" zl_status zl_paged_decode_noalloc(const void* q, const void* k_pool, 
   args.max_blocks = max_blocks_per_seq;
   args.num_blocks = num_blocks;
   args.scale_log2 = resolve_scale(scale, D) * LOG2E;
+  args.inputs_ahead = 0;
   const int grid = nd->num_sms < kNoAllocMaxCtas ? nd->num_sms : kNoAllocMaxCtas;
   using SM = Smem<kWarps, kStages, false>;
-  e = launch_cooperative(paged_decode_bf16_kernel<kWarps, kStages, false>, grid, SM::kTotal, st, args, tk, tv);
+  e = launch_decode(paged_decode_bf16_kernel<kWarps, kStages, false>, grid, SM::kTotal, st, args, tk, tv,
+                    false);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(ZL_ERR_CUDA, "paged_decode_noalloc: launch: %s", cudaGetErrorString(e));
   return ZL_OK;

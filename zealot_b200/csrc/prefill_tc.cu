@@ -147,6 +147,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
   const uint32_t tS[2] = {tmem, tmem + 128};
   const uint32_t tO[2] = {tmem + 256, tmem + 384};
 
+  if (warp < 4) {
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------- producer
     const int y0 = start + BM * t;
@@ -215,7 +216,8 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         }
       }
     }
-  } else if (warp >= 4) {
+  }
+  } else {
     // ------------------------------------------------------ softmax + epilogue
     const int w = (warp - 4) >> 2;             // which query head of the pair
     const int r = 32 * (warp & 3) + lane;      // query row in the tile == TMEM lane
@@ -236,6 +238,111 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
       const bool edge = (j == nkv - 1) && (a.causal || (L % BN) != 0);
       const int key_lim = edge ? (a.causal ? min(q_row + 1, L) : L) - BN * j : BN;
       uint32_t va[32], vb[32];
+      // Speculative single pass (interior tiles after the first): the
+      // exponentials are taken against the running max as it stands while the
+      // tile's own max is tracked alongside, so the max pass (two TMEM loads
+      // and the max chain) leaves the softmax's critical path. The tile is
+      // done in two 64-key halves. If a row of the first half beats the
+      // running max by more than 2^8, nothing has been stored and the
+      // two-pass path below redoes the tile; if only the second half does, the
+      // first half's P (already in TMEM) is re-based to the new max in place.
+      bool done = false;
+      if (j > 0 && !edge) {
+        uint32_t pa[16], pb[16];
+        float mx8[8];
+        uint64_t ls2[4];
+        const uint64_t sc2 = f2_pack(sc, sc);
+        // exponentials of one half against max mref, P packed into pa / pb
+        auto half_exp = [&](float mref) {
+          const uint64_t nm2 = f2_pack(-mref, -mref);
+#pragma unroll
+          for (int u = 0; u < 4; u++) ls2[u] = 0ull;
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float a0 = __uint_as_float(va[2 * i]), a1 = __uint_as_float(va[2 * i + 1]);
+            const float b0 = __uint_as_float(vb[2 * i]), b1 = __uint_as_float(vb[2 * i + 1]);
+            const float2 xa = f2_unpack(f2_fma(f2_pack(a0, a1), sc2, nm2));
+            const float2 xb = f2_unpack(f2_fma(f2_pack(b0, b1), sc2, nm2));
+            const float p0 = ex2(xa.x), p1 = ex2(xa.y), p2 = ex2(xb.x);
+            const float p3 = (i & 1) ? ex2_fma(xb.y) : ex2(xb.y);
+            ls2[(2 * i) & 3] = f2_add(ls2[(2 * i) & 3], f2_pack(p0, p1));
+            ls2[(2 * i + 1) & 3] = f2_add(ls2[(2 * i + 1) & 3], f2_pack(p2, p3));
+            pa[i] = pack_bf16x2(p0, p1);
+            pb[i] = pack_bf16x2(p2, p3);
+          }
+          float ls8[8];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const float2 v = f2_unpack(ls2[u]);
+            ls8[2 * u] = v.x;
+            ls8[2 * u + 1] = v.y;
+          }
+          return ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
+        };
+        auto half_max = [&]() {
+#pragma unroll
+          for (int u = 0; u < 8; u++) mx8[u] = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            mx8[i & 7] = max3(mx8[i & 7], __uint_as_float(va[i]), __uint_as_float(vb[i]));
+          return fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sc;
+        };
+        tmem_ld32(tSr, va);
+        tmem_ld32(tSr + 32, vb);
+        tc_wait_ld();
+        const float ls_a = half_exp(m);
+        const float mt_a = half_max();
+        if (!__any_sync(0xffffffffu, mt_a > m + kLazy)) {
+          tmem_st16(tSr, pa);          // P of keys 0-63 over S columns 0-31
+          tmem_st16(tSr + 16, pb);
+          tmem_ld32(tSr + 64, va);     // S of keys 64-127 (columns 64-127, untouched)
+          tmem_ld32(tSr + 96, vb);
+          tc_wait_ld();
+          float ls_b = half_exp(m);
+          const float mt_b = half_max();
+          float ls_prev = l + ls_a;
+          if (__any_sync(0xffffffffu, mt_b > m + kLazy)) {
+            // rare: the second half moved the max; re-base to it (S of the
+            // second half is reloaded afterwards: its registers are reused)
+            const float m_new = fmaxf(m, mt_b);
+            const float alpha = ex2(m - m_new);  // 1 for rows whose max did not move
+            uint32_t vp[32];
+            tmem_ld32(tSr, vp);                  // the first half's P, bf16 pairs
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vp[i]));
+              vp[i] = pack_bf16x2(f.x * alpha, f.y * alpha);
+            }
+            tmem_st32(tSr, vp);
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {     // O of this row by alpha
+              tmem_ld32(tOr + 64 * hh, va);
+              tmem_ld32(tOr + 64 * hh + 32, vb);
+              tc_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; i++) {
+                va[i] = __float_as_uint(__uint_as_float(va[i]) * alpha);
+                vb[i] = __float_as_uint(__uint_as_float(vb[i]) * alpha);
+              }
+              tmem_st32(tOr + 64 * hh, va);
+              tmem_st32(tOr + 64 * hh + 32, vb);
+            }
+            ls_prev *= alpha;
+            m = m_new;
+            tmem_ld32(tSr + 64, va);
+            tmem_ld32(tSr + 96, vb);
+            tc_wait_ld();
+            ls_b = half_exp(m);
+          }
+          tmem_st16(tSr + 32, pa);     // P of keys 64-127 over S columns 32-63
+          tmem_st16(tSr + 48, pb);
+          l = ls_prev + ls_b;
+          done = true;
+        }
+      }
+      if (!done) {
       // 8 independent max accumulators: a 128-long dependent fmax chain would
       // dominate the row's latency
       float mx8[8];
@@ -328,6 +435,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         }
       }
       m = m_new;
+      }  // two-pass path
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(bar(P_READY + w));

@@ -20,6 +20,7 @@ enum : int {
 
 struct zl_ctx {
   int device = 0;
+  uint32_t flags = 0;             // ZL_CTX_* (zl_ctx_set_flags)
   int num_sms = 148;
   int* d_status = nullptr;        // device status word
   void* workspace = nullptr;      // split-KV partials + per-segment counters

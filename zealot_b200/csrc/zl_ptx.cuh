@@ -80,6 +80,17 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, in
   }
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Lets the next kernel on the stream be scheduled before this one finishes (it
+// still waits in griddep_wait for this grid's completion and memory flush).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Waits until the grids this one depends on (the previous kernel on the stream,
+// when launched with programmatic stream serialization) have completed and
+// their writes are visible; returns at once otherwise.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------- proxies
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
