@@ -86,6 +86,32 @@ def test_bf16_prefill_c3_sampled(ctx, oracle):
     assert np.max(np.abs(got - ref)) <= 2e-2
 
 
+def test_bf16_prefill_max_moves_inside_tiles(ctx, oracle):
+    """Keys scaled far above the rest sit in the second 64-key half of interior
+    tiles (and one in a first half), so for many rows the running max jumps by
+    more than 2^8 inside a tile after its first half has already been handed to
+    the P V products: the O rescale then waits for those products and the
+    second half is taken against the new max. Rows are checked against the oracle."""
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = 32, 8, 128
+    rng = np.random.default_rng(29)
+    lens = [1024, 777]
+    cu, q, k, v = _case(rng, lens, H, Hkv, d)
+    for pos, factor in ((128 + 100, 12.0), (384 + 70, 25.0), (512 + 10, 30.0), (640 + 127, 40.0),
+                        (1024 + 256 + 90, 20.0), (1024 + 512 + 65, 35.0)):
+        k[pos] *= factor
+    tq, q32 = bf16_tensor(oracle, q)
+    tk, k32 = bf16_tensor(oracle, k)
+    tv, v32 = bf16_tensor(oracle, v)
+    out = torch.full_like(tq, float("nan"))
+    zb.CudaAttention(ctx).forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d,
+                                      max(lens), causal=True)
+    ctx.check_status()
+    ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=True, num_threads=8)
+    assert np.max(np.abs(to_f32(out) - ref)) <= 2e-2
+
+
 @pytest.mark.parametrize("path", ["tcgen05", "generic"])
 @pytest.mark.parametrize("bad", ["past_end", "backwards", "longer_than_max"])
 def test_malformed_cu_seqlens_is_reported(ctx, oracle, path, bad):

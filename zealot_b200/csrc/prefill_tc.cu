@@ -172,18 +172,19 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
     }
   } else if (warp == 1 && lane == 0) {
     // ----------------------------------------------------------- MMA issuer
+    // step-0 descriptors of every operand tile, computed once: each group of
+    // eight MMAs is then one asm block (tc_mma_*_k128). The single issuing
+    // thread's dependent instruction chain per MMA (descriptor arithmetic,
+    // predicate, issue) otherwise sets the rate at which products reach the
+    // tensor pipe.
+    const uint64_t dq0 = desc_kmajor(base + Smem::kQ, 0), dq1 = desc_kmajor(base + Smem::kQ + TILE, 0);
+    const uint64_t dk0 = desc_kmajor(base + Smem::kK, 0), dk1 = desc_kmajor(base + Smem::kK + TILE, 0);
+    const uint64_t dv0 = desc_v(base + Smem::kV, 0), dv1 = desc_v(base + Smem::kV + TILE, 0);
     auto issue_s = [&](int w, int st) {
-      const uint32_t q = base + Smem::kQ + w * TILE;
-      const uint32_t k = base + Smem::kK + st * TILE;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; kk++)
-        tc_mma_ss(tS[w], desc_kmajor(q, kk), desc_kmajor(k, kk), IDESC_S, kk > 0);
+      tc_mma_ss_k128(tS[w], w ? dq1 : dq0, st ? dk1 : dk0, IDESC_S, 0u);
     };
     auto issue_pv = [&](int w, int st, bool acc) {
-      const uint32_t v = base + Smem::kV + st * TILE;
-#pragma unroll
-      for (int kk = 0; kk < BN / 16; kk++)
-        tc_mma_ts(tO[w], tS[w] + kk * 8, desc_v(v, kk), IDESC_PV, (acc || kk > 0) ? 1u : 0u);
+      tc_mma_ts_k128(tO[w], tS[w], st ? dv1 : dv0, IDESC_PV, acc ? 1u : 0u);
     };
     bool ok = mbar_wait(bar(Q_FULL), 0, a.status) && mbar_wait(bar(K_FULL), 0, a.status);
     if (ok) {

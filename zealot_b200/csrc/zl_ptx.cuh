@@ -230,6 +230,68 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Eight kind::f16 MMAs over a 128-deep K extent from one asm block. A and B
+// are K-major in 128-byte-swizzled boxes of 64 columns: k-step kk starts 32 B
+// further inside a box and the second box 16 KB on, so each step's descriptor
+// is the step-0 descriptor plus a constant in its start-address field (>> 4).
+// The single issuing thread's dependent instruction chain per MMA sets the
+// issue rate, so the offsets are independent adds and the accumulate
+// predicates are set once for the group. acc_first: the first step
+// accumulates into D (the later steps always do).
+__device__ __forceinline__ void tc_mma_ss_k128(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      ".reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "add.s64 a1, %1, 2;\n\t" "add.s64 b1, %2, 2;\n\t"
+      "add.s64 a2, %1, 4;\n\t" "add.s64 b2, %2, 4;\n\t"
+      "add.s64 a3, %1, 6;\n\t" "add.s64 b3, %2, 6;\n\t"
+      "add.s64 a4, %1, 1024;\n\t" "add.s64 b4, %2, 1024;\n\t"
+      "add.s64 a5, %1, 1026;\n\t" "add.s64 b5, %2, 1026;\n\t"
+      "add.s64 a6, %1, 1028;\n\t" "add.s64 b6, %2, 1028;\n\t"
+      "add.s64 a7, %1, 1030;\n\t" "add.s64 b7, %2, 1030;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc_first)
+      : "memory");
+}
+// Eight MMAs D (+)= A[tmem] * B over 128 keys: A is 16 key columns of bf16
+// pairs per step (8 TMEM columns), B an MN-major 128-byte-swizzled operand
+// whose k-step kk starts 2 KB further (the same single-block form as above).
+__device__ __forceinline__ void tc_mma_ts_k128(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      ".reg .b32 a1, a2, a3, a4, a5, a6, a7;\n\t"
+      ".reg .b64 b1, b2, b3, b4, b5, b6, b7;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "add.u32 a1, %1, 8;\n\t" "add.s64 b1, %2, 128;\n\t"
+      "add.u32 a2, %1, 16;\n\t" "add.s64 b2, %2, 256;\n\t"
+      "add.u32 a3, %1, 24;\n\t" "add.s64 b3, %2, 384;\n\t"
+      "add.u32 a4, %1, 32;\n\t" "add.s64 b4, %2, 512;\n\t"
+      "add.u32 a5, %1, 40;\n\t" "add.s64 b5, %2, 640;\n\t"
+      "add.u32 a6, %1, 48;\n\t" "add.s64 b6, %2, 768;\n\t"
+      "add.u32 a7, %1, 56;\n\t" "add.s64 b7, %2, 896;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc_first)
+      : "memory");
+}
 // Arrives on `bar` once every previously issued tcgen05.mma of this thread completes.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
