@@ -347,7 +347,10 @@ typedef struct {
   const void* w_down;     /* [hidden][inter]                                  */
 } zl_layer_weights;
 /* When wk starts where wq ends and wv where wk ends (one [(H+2*Hkv)*d][hidden]
- * buffer), steps of at most 256 rows compute q, k and v with one GEMM. */
+ * buffer), steps of at most 256 rows compute q, k and v with one GEMM. Steps of
+ * at least 512 rows compute gate/up and silu(gate)*up with zl_linear_swiglu
+ * (hidden % 64 == 0, inter % 128 == 0): gate/up is then not rounded to bf16
+ * before the activation. */
 
 typedef struct {
   int num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate;
@@ -376,6 +379,19 @@ typedef struct {
   const int32_t* last_rows;    /* [num_last] rows whose logits are produced     */
   int num_last;
 } zl_step_batch;
+
+/* The MLP's gate/up projection with the activation fused into it:
+ * out[t][i] = silu(x[t] . w[i]) * (x[t] . w[I + i]) for x [M][K], w_gate_up
+ * [2I][K] (gate rows, then up rows), out [M][I], all bf16, fp32 accumulation
+ * on the tcgen05 tensor cores; silu(g) * u is taken from the fp32 accumulators
+ * and rounded once, and the [M][2I] gate/up product never reaches HBM.
+ * Replaces the gate and up GEMMs and silu_gate_mul of the reference runner
+ * (src/cuda_runner.rs:529-572, src/attention/kernels/activation.cu:4-12).
+ * K % 64 == 0, I % 128 == 0 and 16-byte aligned buffers, else
+ * ZL_ERR_UNSUPPORTED; M == 0 is a no-op. zl_decoder_step uses it for every
+ * layer whose shapes allow it. */
+zl_status zl_linear_swiglu(zl_ctx* ctx, const void* x, const void* w_gate_up, void* out, int64_t M, int K,
+                           int I, zl_stream stream);
 
 /* ---------------------------------------------------------------------------
  * Sampling on the GPU for every row of a step: Sampler::sample_with_mask

@@ -140,6 +140,7 @@ SIGNATURES = {
     "zl_decode_graph_tokens": (c_int, [c_void_p, P(c_int64), P(c_float)]),
     "zl_decode_graph_logits": (c_int, [c_void_p, P(c_float)]),
     "zl_decode_graph_num_kernels": (c_int, [c_void_p]),
+    "zl_linear_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p]),
     "zl_decoder_step": (c_int, [c_void_p, P(zl_decoder), P(c_void_p), P(c_void_p), c_int64, c_int,
                                 P(zl_step_batch), c_void_p, c_void_p]),
 }

@@ -111,6 +111,10 @@ zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const voi
                             int64_t total_tokens, void* out,
                             int H, int Hkv, int d, float scale, int causal, zl_gqa_map map,
                             cudaStream_t st);
+// Gate/up projection with the SwiGLU epilogue (gemm_swiglu.cu); ZL_ERR_UNSUPPORTED
+// outside its shape envelope (K % 64, I % 128, 16-byte alignment).
+zl_status launch_gemm_swiglu(zl_ctx* ctx, const void* x, const void* w, void* out, int64_t M, int K, int I,
+                             cudaStream_t st);
 zl_status launch_merge(zl_ctx* ctx, const float* m, const float* l, const float* o, int P,
                        int64_t rows, int d, void* out, zl_dtype dtype, cudaStream_t st);
 zl_status launch_embedding_gather(zl_ctx* ctx, const int64_t* ids, int64_t n, const float* table,
