@@ -269,6 +269,11 @@ def run_ours(args, rank, world, local_rank):
                            num_blocks=pool_blocks, stream=s_handle)
 
     # ---- device-resident timing, clocks sampled over a ~1 s soak and the timed steps
+    # The tables and lengths were written once before any timed kernel, so the
+    # decode may read them before its dependency wait (ZL_CTX_INPUTS_AHEAD); the
+    # e2e loop below uploads them every step and runs with the flag off.
+    from zealot_b200.context import CTX_INPUTS_AHEAD
+    ctx.set_flags(CTX_INPUTS_AHEAD)
     for k in range(args.warmup):
         step(k)
     ctx.check_status(s_handle)
@@ -329,6 +334,7 @@ def run_ours(args, rank, world, local_rank):
             h_out[b].copy_(d_out[b], non_blocking=True)
             ev_free[b].record(s_out)
 
+    ctx.set_flags(0)
     e2e = None
     e2e_launches = 0
     if not args.lite:
@@ -385,7 +391,9 @@ def run_ours(args, rank, world, local_rank):
                    "global_batch": B, "seq_len": 131072,
                    "parallelism": f"kv-head groups x{world} of the fixed job (rank r: kv heads "
                                   f"[r*{hkv_l}, (r+1)*{hkv_l})), split-KV inside each GPU",
-                   "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU"}
+                   "l2": f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU",
+                   "launch": "device-resident steps with zl_ctx_set_flags(ZL_CTX_INPUTS_AHEAD) (tables and "
+                             "lengths written once before timing); e2e steps upload them and run without it"}
         else:
             l2 = (f"inputs larger than L2: {alg / 1e6:.0f} MB of KV read per step per GPU" if n_sets == 1 else
                   f"{alg / 1e6:.0f} MB of KV per step per GPU; steps rotate over {n_sets} block-table sets on "
@@ -396,7 +404,9 @@ def run_ours(args, rank, world, local_rank):
                    "global_batch": B, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
                    "parallelism": f"kv-head groups x{world} of the fixed 64-sequence job (rank r: kv heads "
                                   f"[r*{hkv_l}, (r+1)*{hkv_l}) and query heads [r*{h_l}, (r+1)*{h_l}))",
-                   "l2": l2}
+                   "l2": l2,
+                   "launch": "device-resident steps with zl_ctx_set_flags(ZL_CTX_INPUTS_AHEAD) (tables and "
+                             "lengths written once before timing); e2e steps upload them and run without it"}
         line = {
             "metric": "paged_decode_tokens_per_s",
             "value": round(tokens_per_s, 1),
@@ -464,7 +474,10 @@ def measure_c5(args, R, ctx, attn, stream, peaks):
     def head_step(k):
         attn.paged_forward(qc, kc, vc, tt, tl, oc, B, hhi - hlo, hi - lo, D, BS, MAXB, num_blocks=nb, stream=sh)
 
+    from zealot_b200.context import CTX_INPUTS_AHEAD
+    ctx.set_flags(CTX_INPUTS_AHEAD)  # static tables, written before any timed kernel
     ms, ms_r, _ = timed_loop(R, stream, ctx, head_step, args.steps, args.warmup)
+    ctx.set_flags(0)
     alg = algorithmic_bytes(lens, hi - lo, hhi - hlo)
     res = {"c5": {"workload": "C5: 8 x 131072 tokens, 64 q / 8 kv heads, d 128, bf16; kv heads sharded over "
                               f"{world} GPU(s) (rank r: kv heads [r*{hi - lo}, (r+1)*{hi - lo})), split-KV inside "

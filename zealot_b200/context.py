@@ -8,6 +8,9 @@ from .errors import check
 
 GQA_GROUPED = 0  # kv = h / (H / Hkv)   (paged_attention.cu:32)
 GQA_MODULO = 1   # kv = h % Hkv         (model_runner_cpu.rs:295)
+# zl_ctx_set_flags: block tables, seq_lens and token ranges of later decode calls
+# are written before the kernel that precedes the decode on its stream starts
+CTX_INPUTS_AHEAD = 1
 
 F32 = 0
 BF16 = 1
@@ -78,6 +81,12 @@ class GpuContext:
 
     def launch_count(self) -> int:
         return int(self.lib.zl_launch_count(self.handle))
+
+    def set_flags(self, flags: int) -> None:
+        """zl_ctx_set_flags: CTX_INPUTS_AHEAD lets the decode kernel read its
+        tables and lengths before waiting for the preceding kernel on its stream
+        (only when they were written before that kernel started)."""
+        check(self.lib.zl_ctx_set_flags(self.handle, flags))
 
     def close(self) -> None:
         if getattr(self, "handle", None):

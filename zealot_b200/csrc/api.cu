@@ -113,8 +113,11 @@ zl_status zl_ctx_create(const zl_ctx_cfg* cfg, zl_ctx** out) {
                      dev, prop.major, prop.minor);
   }
   ctx->num_sms = prop.multiProcessorCount;
-  e = cudaMalloc(&ctx->d_status, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(int));
+  // status word at [0]; the persistent prefill's two work counters at [32], a
+  // 128-byte line of their own
+  e = cudaMalloc(&ctx->d_status, 64 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, 64 * sizeof(int));
+  ctx->prefill_work = ctx->d_status + 32;
   if (e != cudaSuccess) { delete ctx; return set_error(ZL_ERR_CUDA, "status word: %s", cudaGetErrorString(e)); }
   if (cfg && cfg->workspace_bytes) {
     s = ensure_workspace(ctx, cfg->workspace_bytes);
@@ -165,6 +168,7 @@ zl_status zl_check_status(zl_ctx* ctx, zl_stream stream) {
     // A kernel that gave up may have left split-KV counters mid-count.
     ZL_CUDA_TRY(cudaMemset(ctx->counters, 0, ctx->counters_bytes));
   }
+  if (h) ZL_CUDA_TRY(cudaMemset(ctx->prefill_work, 0, 2 * sizeof(int)));
   if (h & ZL_DEV_TIMEOUT) return set_error(ZL_ERR_TIMEOUT, "a bounded device wait ran out (status 0x%x)", h);
   if (h & ZL_DEV_OOB)
     return set_error(ZL_ERR_OOB_BLOCK, "a block id or slot was outside the pool (status 0x%x)", h);

@@ -5,9 +5,13 @@
 // of the reference: scalar fp32 FMAs over shared memory, one sequence in
 // [H][L][d]) for packed varlen input q [T][H][128], k/v [T][Hkv][128].
 //
-// One CTA owns a 128-row query tile of one sequence for TWO query heads of the
-// same kv group, so every K/V tile it loads feeds two score tiles:
-//   warp 0      TMA producer: Q tiles once, K/V tiles through a 2-stage ring
+// A work item is a 128-row query tile of one sequence for TWO query heads of
+// the same kv group, so every K/V tile it loads feeds two score tiles. The
+// kernel is persistent (one CTA per SM); items are taken heaviest first from a
+// device counter, and the next item's Q load and first score products overlap
+// the current item's last tiles and epilogue:
+//   warp 0      work fetch + TMA producer: Q tiles once per item, K/V tiles
+//               through a 2-stage ring
 //   warp 1      MMA issuer (one thread) + TMEM owner (alloc/dealloc 512 cols)
 //   warps 4-7   softmax warpgroup for head 0, one thread per query row
 //   warps 8-11  softmax warpgroup for head 1
@@ -41,15 +45,22 @@ constexpr int HALF = TILE / 2;
 constexpr int THREADS = 384;
 constexpr float LOG2E = 1.4426950408889634f;
 
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_READY = 11,
-           O_FINAL = 13, NUM_BARS = 15 };
+// Per item: Q_FULL / Q_EMPTY (the item's Q tiles loaded / its last score
+// products done, so the next item's Q may land), O_FINAL (the item's last
+// P V done), O_EMPTY (the epilogue has read O: the next item's first P V may
+// overwrite it). Per tile (running count across items): K/V ring, S_FULL,
+// P_READY. IT_FULL / IT_EMPTY: a 2-slot ring of fetched item ids.
+enum Bar { Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, K_EMPTY = 4, V_FULL = 6, V_EMPTY = 8, S_FULL = 10,
+           P_READY = 12, O_FINAL = 14, O_EMPTY = 16, IT_FULL = 18, IT_EMPTY = 20, NUM_BARS = 22 };
+constexpr int IT_READERS = 1 + 8;  // the MMA thread and one lane of each softmax warp
 
 struct Smem {
   static constexpr int kQ = 0;                      // NQ tiles
   static constexpr int kK = kQ + NQ * TILE;         // 2 stages
   static constexpr int kV = kK + 2 * TILE;          // 2 stages
   static constexpr int kBars = kV + 2 * TILE;
-  static constexpr int kTmem = kBars + NUM_BARS * 8;
+  static constexpr int kItems = kBars + NUM_BARS * 8;  // 2 fetched item ids
+  static constexpr int kTmem = kItems + 8;
   static constexpr int kTotal = 1024 + kTmem + 16;
 };
 
@@ -57,11 +68,43 @@ struct PrefillArgs {
   const int32_t* cu_seqlens;
   __nv_bfloat16* out;  // [T][H][D]
   int* status;
+  int* work;             // [0] next item, [1] CTAs finished; zero between launches
   int64_t total_tokens;  // rows of q / k / v / out: every sequence must end at or before it
   int H, Hkv, G, num_seqs;
+  int hp_count, max_tiles, total_items;
   float scale_log2;
   int causal;
 };
+
+// Item idx -> (sequence, head pair, query tile); items run heaviest (latest
+// tile) first. nkv: K/V tiles to visit; 0 = the tile is past the sequence;
+// -1 = cu_seqlens is malformed for this sequence.
+struct Item {
+  int s, hp, t, start, L, nkv;
+};
+__device__ __forceinline__ Item decode_item(const PrefillArgs& a, int idx) {
+  Item it;
+  const int xy = a.num_seqs * a.hp_count;
+  const int y = idx / xy, x = idx - y * xy;
+  it.t = a.max_tiles - 1 - y;
+  it.s = x / a.hp_count;
+  it.hp = x - it.s * a.hp_count;
+  it.start = a.cu_seqlens[it.s];
+  const int end = a.cu_seqlens[it.s + 1];
+  it.L = end - it.start;
+  // cu_seqlens comes from device memory: a sequence outside [0, total_tokens]
+  // or running backwards is reported and skipped, so no load or store leaves
+  // the caller's buffers. A sequence longer than the launch's max_seq_len
+  // (rows no tile covers) is reported and skipped too.
+  if (it.start < 0 || end < it.start || (int64_t)end > a.total_tokens ||
+      (int64_t)it.L > (int64_t)BM * a.max_tiles)
+    it.nkv = -1;
+  else if (BM * it.t >= it.L)
+    it.nkv = 0;
+  else
+    it.nkv = a.causal ? it.t + 1 : (it.L + BN - 1) / BN;
+  return it;
+}
 
 constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, false, false);
 constexpr uint32_t IDESC_PV = idesc_bf16(BM, D, false, true);
@@ -95,39 +138,20 @@ __device__ __forceinline__ float ex2_fma(float x) {
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
                   const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV) {
-  const int hp_count = a.H / NQ;
-  const int s = blockIdx.x / hp_count;
-  const int hp = blockIdx.x - s * hp_count;
-  const int t = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles launch first
-  const int start = a.cu_seqlens[s];
-  const int end = a.cu_seqlens[s + 1];
-  // cu_seqlens comes from device memory: a sequence outside [0, total_tokens]
-  // or running backwards is reported and skipped, so no load or store leaves
-  // the caller's buffers. A sequence longer than the launch's max_seq_len
-  // (rows no tile covers) is reported and skipped too. Uniform over the CTA.
-  if (start < 0 || end < start || (int64_t)end > a.total_tokens ||
-      (int64_t)(end - start) > (int64_t)BM * gridDim.y) {
-    if (threadIdx.x == 0 && blockIdx.y == 0) atomicOr(a.status, ZL_DEV_OOB);
-    return;
-  }
-  const int L = end - start;
-  if (BM * t >= L) return;  // uniform: this tile is past the sequence
-  if (aborted(a.status)) return;  // an earlier CTA timed out: do not queue behind it
-  const int h0 = hp * NQ;
-  const int kvh = h0 / a.G;
-  const int nkv = a.causal ? t + 1 : (L + BN - 1) / BN;
-
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* sbase = smem_raw + (base - raw);
   auto bar = [&](int i) { return base + Smem::kBars + 8 * i; };
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sbase + Smem::kTmem);
+  volatile int* items = reinterpret_cast<volatile int*>(sbase + Smem::kItems);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < NUM_BARS; i++) {
-      const int count = (i == P_READY || i == P_READY + 1) ? 128 : 1;
+      int count = 1;
+      if (i == P_READY || i == P_READY + 1 || i == O_EMPTY || i == O_EMPTY + 1) count = 128;
+      if (i == IT_EMPTY || i == IT_EMPTY + 1) count = IT_READERS;
       mbar_init(bar(i), count);
     }
     fence_mbar_init();
@@ -149,26 +173,46 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
 
   if (warp < 4) {
   if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------- producer
-    const int y0 = start + BM * t;
-    mbar_arrive_expect_tx(bar(Q_FULL), NQ * TILE);
-    for (int w = 0; w < NQ; w++) {
-      const uint32_t dst = base + Smem::kQ + w * TILE;
-      tma_load_2d(dst, &tmQ, (h0 + w) * D, y0, bar(Q_FULL));
-      tma_load_2d(dst + HALF, &tmQ, (h0 + w) * D + 64, y0, bar(Q_FULL));
-    }
-    for (int j = 0; j < nkv; j++) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      const int y = start + BN * j;
-      if (!mbar_wait(bar(K_EMPTY + st), ph ^ 1, a.status)) break;
-      mbar_arrive_expect_tx(bar(K_FULL + st), TILE);
-      tma_load_2d(base + Smem::kK + st * TILE, &tmK, kvh * D, y, bar(K_FULL + st));
-      tma_load_2d(base + Smem::kK + st * TILE + HALF, &tmK, kvh * D + 64, y, bar(K_FULL + st));
-      if (!mbar_wait(bar(V_EMPTY + st), ph ^ 1, a.status)) break;
-      mbar_arrive_expect_tx(bar(V_FULL + st), TILE);
-      tma_load_2d(base + Smem::kV + st * TILE, &tmV, kvh * D, y, bar(V_FULL + st));
-      tma_load_2d(base + Smem::kV + st * TILE + HALF, &tmV, kvh * D + 64, y, bar(V_FULL + st));
+    // ------------------------------------------------- work fetch + producer
+    // Item k goes to slot k & 1 of the item ring; the id past the last item
+    // (or once a wait anywhere timed out) tells the other roles to stop.
+    int q_it = 0, g = 0;  // items with work, K/V tiles loaded (running counts)
+    for (int k = 0;; k++) {
+      const int slot = k & 1;
+      if (!mbar_wait(bar(IT_EMPTY + slot), ((k >> 1) & 1) ^ 1, a.status)) break;
+      const int idx = aborted(a.status) ? a.total_items : atomicAdd(a.work, 1);
+      items[slot] = idx < a.total_items ? idx : a.total_items;
+      mbar_arrive(bar(IT_FULL + slot));  // release: the id is visible to the waiters
+      if (idx >= a.total_items) break;
+      const Item it = decode_item(a, idx);
+      if (it.nkv < 0) atomicOr(a.status, ZL_DEV_OOB);
+      if (it.nkv <= 0) continue;
+      const int h0 = it.hp * NQ, kvh = h0 / a.G;
+      // the Q buffer is free once the previous item's last score products are done
+      if (!mbar_wait(bar(Q_EMPTY), (q_it & 1) ^ 1, a.status)) break;
+      const int y0 = it.start + BM * it.t;
+      mbar_arrive_expect_tx(bar(Q_FULL), NQ * TILE);
+      for (int w = 0; w < NQ; w++) {
+        const uint32_t dst = base + Smem::kQ + w * TILE;
+        tma_load_2d(dst, &tmQ, (h0 + w) * D, y0, bar(Q_FULL));
+        tma_load_2d(dst + HALF, &tmQ, (h0 + w) * D + 64, y0, bar(Q_FULL));
+      }
+      bool ok = true;
+      for (int j = 0; j < it.nkv; j++, g++) {
+        const int st = g & 1;
+        const uint32_t ph = (g >> 1) & 1;
+        const int y = it.start + BN * j;
+        if (!(ok = mbar_wait(bar(K_EMPTY + st), ph ^ 1, a.status))) break;
+        mbar_arrive_expect_tx(bar(K_FULL + st), TILE);
+        tma_load_2d(base + Smem::kK + st * TILE, &tmK, kvh * D, y, bar(K_FULL + st));
+        tma_load_2d(base + Smem::kK + st * TILE + HALF, &tmK, kvh * D + 64, y, bar(K_FULL + st));
+        if (!(ok = mbar_wait(bar(V_EMPTY + st), ph ^ 1, a.status))) break;
+        mbar_arrive_expect_tx(bar(V_FULL + st), TILE);
+        tma_load_2d(base + Smem::kV + st * TILE, &tmV, kvh * D, y, bar(V_FULL + st));
+        tma_load_2d(base + Smem::kV + st * TILE + HALF, &tmV, kvh * D + 64, y, bar(V_FULL + st));
+      }
+      if (!ok) break;
+      q_it++;
     }
   } else if (warp == 1 && lane == 0) {
     // ----------------------------------------------------------- MMA issuer
@@ -186,36 +230,58 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
     auto issue_pv = [&](int w, int st, bool acc) {
       tc_mma_ts_k128(tO[w], tS[w], st ? dv1 : dv0, IDESC_PV, acc ? 1u : 0u);
     };
-    bool ok = mbar_wait(bar(Q_FULL), 0, a.status) && mbar_wait(bar(K_FULL), 0, a.status);
-    if (ok) {
+    int q_it = 0, g = 0;  // items with work, tiles (running counts)
+    bool ok = true;
+    for (int k = 0; ok; k++) {
+      const int slot = k & 1;
+      if (!(ok = mbar_wait(bar(IT_FULL + slot), (k >> 1) & 1, a.status))) break;
+      const int idx = items[slot];
+      mbar_arrive(bar(IT_EMPTY + slot));
+      if (idx >= a.total_items) break;
+      const Item it = decode_item(a, idx);
+      if (it.nkv <= 0) continue;
+      const int nkv = it.nkv;
+      // S(0) of both heads: the S columns are free (this thread issued the
+      // previous item's last P V before, and the products complete in order)
+      if (!(ok = mbar_wait(bar(Q_FULL), q_it & 1, a.status))) break;
+      if (!(ok = mbar_wait(bar(K_FULL + (g & 1)), (g >> 1) & 1, a.status))) break;
       tc_fence_after();
       for (int w = 0; w < NQ; w++) {
-        issue_s(w, 0);
+        issue_s(w, g & 1);
         tc_commit(bar(S_FULL + w));
       }
-      tc_commit(bar(K_EMPTY));
-    }
-    for (int j = 0; ok && j < nkv; j++) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      const int st1 = (j + 1) & 1;
-      const uint32_t ph1 = ((j + 1) >> 1) & 1;
-      if (!(ok = mbar_wait(bar(V_FULL + st), ph, a.status))) break;
-      for (int w = 0; w < NQ && ok; w++) {
-        if (!(ok = mbar_wait(bar(P_READY + w), j & 1, a.status))) break;
-        tc_fence_after();
-        issue_pv(w, st, j > 0);
-        if (w == NQ - 1) tc_commit(bar(V_EMPTY + st));
-        if (j + 1 < nkv) {
-          if (w == 0 && !(ok = mbar_wait(bar(K_FULL + st1), ph1, a.status))) break;
+      tc_commit(bar(K_EMPTY + (g & 1)));
+      if (nkv == 1) tc_commit(bar(Q_EMPTY));  // every score product of this item issued
+      for (int j = 0; ok && j < nkv; j++) {
+        const int gj = g + j;
+        const int st = gj & 1;
+        const uint32_t ph = (gj >> 1) & 1;
+        const int st1 = (gj + 1) & 1;
+        const uint32_t ph1 = ((gj + 1) >> 1) & 1;
+        if (!(ok = mbar_wait(bar(V_FULL + st), ph, a.status))) break;
+        for (int w = 0; w < NQ && ok; w++) {
+          if (!(ok = mbar_wait(bar(P_READY + w), gj & 1, a.status))) break;
+          // the first P V of an item overwrites O: the previous item's epilogue must have read it
+          if (j == 0 && q_it > 0 && !(ok = mbar_wait(bar(O_EMPTY + w), (q_it - 1) & 1, a.status))) break;
           tc_fence_after();
-          issue_s(w, st1);
-          tc_commit(bar(S_FULL + w));
-          if (w == NQ - 1) tc_commit(bar(K_EMPTY + st1));
-        } else {
-          tc_commit(bar(O_FINAL + w));
+          issue_pv(w, st, j > 0);
+          if (w == NQ - 1) tc_commit(bar(V_EMPTY + st));
+          if (j + 1 < nkv) {
+            if (w == 0 && !(ok = mbar_wait(bar(K_FULL + st1), ph1, a.status))) break;
+            tc_fence_after();
+            issue_s(w, st1);
+            tc_commit(bar(S_FULL + w));
+            if (w == NQ - 1) {
+              tc_commit(bar(K_EMPTY + st1));
+              if (j + 2 == nkv) tc_commit(bar(Q_EMPTY));
+            }
+          } else {
+            tc_commit(bar(O_FINAL + w));
+          }
         }
       }
+      g += nkv;
+      q_it++;
     }
   }
   } else {
@@ -224,16 +290,27 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
     const int r = 32 * (warp & 3) + lane;      // query row in the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t tSr = tS[w] + lane_off, tOr = tO[w] + lane_off;
-    const int q_row = BM * t + r;              // row index within the sequence
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
     // The running max only moves when a tile's row max exceeds it by more
     // than 2^8: until then p = 2^(s - m) <= 256 is exact enough in bf16/fp32
     // and the O rescale (a TMEM round trip of 128 columns) is skipped.
     constexpr float kLazy = 8.f;
     const float sc = a.scale_log2;
+    bool ok = true;
+    int q_it = 0, g = 0;  // items with work, tiles (running counts)
+    for (int k = 0; ok; k++) {
+    const int slot = k & 1;
+    if (!(ok = mbar_wait_warp(bar(IT_FULL + slot), (k >> 1) & 1, a.status))) break;
+    const int idx = items[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(IT_EMPTY + slot));
+    if (idx >= a.total_items) break;
+    const Item it = decode_item(a, idx);
+    if (it.nkv <= 0) continue;
+    const int t = it.t, L = it.L, start = it.start, nkv = it.nkv, h0 = it.hp * NQ;
+    const int q_row = BM * t + r;              // row index within the sequence
+    float m = -INFINITY, l = 0.f;
     for (int j = 0; j < nkv; j++) {
-      if (!(ok = mbar_wait_warp(bar(S_FULL + w), j & 1, a.status))) break;
+      if (!(ok = mbar_wait_warp(bar(S_FULL + w), (g + j) & 1, a.status))) break;
       tc_fence_after();
       // only the last tile of a row range needs a mask (the diagonal when causal)
       const bool edge = (j == nkv - 1) && (a.causal || (L % BN) != 0);
@@ -441,7 +518,9 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
       tc_fence_before();
       mbar_arrive(bar(P_READY + w));
     }
-    if (ok && mbar_wait_warp(bar(O_FINAL + w), 0, a.status)) {
+    if (!ok) break;
+    if (!(ok = mbar_wait_warp(bar(O_FINAL + w), q_it & 1, a.status))) break;
+    {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = q_row < L;
@@ -462,6 +541,12 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         }
       }
     }
+    // O has been read: the next item's first P V may overwrite it
+    tc_fence_before();
+    mbar_arrive(bar(O_EMPTY + w));
+    g += nkv;
+    q_it++;
+    }  // item loop
   }
   __syncwarp();  // lanes of warps 0 and 1 arrive from different roles
   tc_fence_before();
@@ -472,6 +557,16 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0) {
+    // Every CTA has stopped taking items once it gets here; the last one to
+    // finish returns the work counters to zero for the next launch. (Launches
+    // on one context must not overlap: they share these counters.)
+    __threadfence();
+    if (atomicAdd(a.work + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(a.work, 0);
+      atomicExch(a.work + 1, 0);
+    }
   }
 }
 
@@ -491,7 +586,7 @@ zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const voi
        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) & 15)
     return ZL_ERR_UNSUPPORTED;
   const int max_tiles = (max_seq_len + BM - 1) / BM;
-  if (max_tiles > 65535) return ZL_ERR_UNSUPPORTED;
+  if (max_tiles <= 0 || (int64_t)max_tiles * num_seqs * (H / NQ) >= (1ll << 31)) return ZL_ERR_UNSUPPORTED;
   CUtensorMap tq, tk, tv;
   zl_status s = make_tmap_bf16(&tq, q, (uint64_t)H * D, total_tokens, (uint64_t)H * D * 2, 64, BM);
   if (s != ZL_OK) return s;
@@ -501,10 +596,14 @@ zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const voi
   args.cu_seqlens = cu_seqlens;
   args.out = (__nv_bfloat16*)out;
   args.status = ctx->d_status;
+  args.work = ctx->prefill_work;
   args.total_tokens = total_tokens;
   args.H = H; args.Hkv = Hkv; args.G = H / Hkv; args.num_seqs = num_seqs;
   args.scale_log2 = scale * LOG2E;
   args.causal = causal ? 1 : 0;
+  args.hp_count = H / NQ;
+  args.max_tiles = max_tiles;
+  args.total_items = (int)((int64_t)max_tiles * num_seqs * args.hp_count);
   // the shared-memory limit is a per-device attribute of the function
   static std::atomic<uint64_t> attr_set{0};
   if (ctx->device < 64 && !(attr_set.load() & (1ull << ctx->device))) {
@@ -512,7 +611,7 @@ zl_status launch_prefill_tc(zl_ctx* ctx, const void* q, const void* k, const voi
                                      Smem::kTotal));
     attr_set.fetch_or(1ull << ctx->device);
   }
-  dim3 grid((unsigned)(num_seqs * (H / NQ)), (unsigned)max_tiles);
+  const int grid = args.total_items < ctx->num_sms ? args.total_items : ctx->num_sms;
   prefill_tc_kernel<<<grid, THREADS, Smem::kTotal, st>>>(args, tq, tk, tv);
   ZL_LAUNCH_CHECK(ctx);
   return ZL_OK;

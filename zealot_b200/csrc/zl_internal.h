@@ -23,6 +23,8 @@ struct zl_ctx {
   uint32_t flags = 0;             // ZL_CTX_* (zl_ctx_set_flags)
   int num_sms = 148;
   int* d_status = nullptr;        // device status word
+  int* prefill_work = nullptr;    // [0] next work item, [1] CTAs finished: the persistent prefill's
+                                  // counters (zero between launches; in the status allocation)
   void* workspace = nullptr;      // split-KV partials + per-segment counters
   size_t workspace_bytes = 0;
   void* counters = nullptr;       // zeroed int32 counters, self-resetting
