@@ -382,6 +382,16 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.empty_cache()
         extra.update(measure_c3(args, R, ctx, attn, stream, peaks))
         torch.cuda.empty_cache()
+        if world == 1:
+            # the engine step (C4) and its steady decode loop on one GPU, each with
+            # ~160 GB of weights and paged KV: bounded step counts; a box without the
+            # memory (or any failure) records why instead of failing the line
+            for key, fn, n in (("c4", measure_c4, 5), ("decode_loop", measure_decode_loop, 10)):
+                try:
+                    extra[key] = fn(n, 3)
+                except (Exception, SystemExit) as ex:
+                    extra[key] = {"skipped": f"{type(ex).__name__}: {ex}"[:300]}
+                torch.cuda.empty_cache()
 
     if rank == 0:
         tokens_per_s = B / (ms_step * 1e-3)
@@ -622,7 +632,13 @@ C4 = dict(prefill_chunks=8, chunk_len=512, decode_seqs=248, ctx=(1024, 8192), se
 
 
 def run_c4(args):
-    """--workload c4: one engine step of a Mistral-7B-shaped decoder (32 layers,
+    """--workload c4: the engine-step line (measure_c4)."""
+    line = measure_c4(args.steps, args.warmup)
+    print(json.dumps(line), flush=True)
+
+
+def measure_c4(steps, warmup):
+    """One engine step of a Mistral-7B-shaped decoder (32 layers,
     d_model 4096, 32/8 heads, d 128, intermediate 14336, vocab 32000, random bf16
     weights): 8 prefill chunks x 512 tokens + 248 decode sequences with context
     U{1024..8192}, batched into one zl_decoder_step. tokens/s = rows per step / step
@@ -643,7 +659,7 @@ def run_c4(args):
     need = 2 * cfg.num_layers * pool_bytes + weight_bytes + (4 << 30)
     free, _ = torch.cuda.mem_get_info(0)
     if free < need:
-        raise SystemExit(f"c4 needs {need / 1e9:.1f} GB of device memory, {free / 1e9:.1f} GB free")
+        raise RuntimeError(f"c4 needs {need / 1e9:.1f} GB of device memory, {free / 1e9:.1f} GB free")
     perm = rng.permutation(nblk).astype(np.int32)
     mb = int(nblk_dec.max())
     dtab = np.full((len(dlens), mb), -1, np.int32)
@@ -679,7 +695,7 @@ def run_c4(args):
     def step():
         dec.step(batch, kps, vps, BS, logits=logits, stream=sh)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     ctx.check_status(sh)
     clocks = ClockSampler(0)
@@ -688,12 +704,12 @@ def run_c4(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record(stream)
     e1.synchronize()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / steps
     launches = ctx.launch_count() - launches0
     ctx.check_status(sh)
 
@@ -742,8 +758,7 @@ def run_c4(args):
     sout = sampler.launch(sbatch, logits, unif, stream=sh)
     ms_sample = time_it(lambda: sampler.launch(sbatch, logits, unif, out=sout, stream=sh), n=10)
     # the same rows on the host: the restated reference sampler, a bounded sample of rows
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as _oracle
+    from oracle import oracle as _oracle
     host_logits_np = logits.cpu().numpy()
     ur = unif.cpu().numpy()
     n_cpu = 24
@@ -768,7 +783,7 @@ def run_c4(args):
     kv_bytes = cfg.num_layers * float(dlens.astype(np.int64).sum()) * Hk * d * 2 * 2
     ideal_ms = 1e3 * ((gemm_flop + pre_flop) / (peaks["bf16_tflops"] * 1e12) + kv_bytes / (peaks["hbm_gbs"] * 1e9))
     line = {"metric": "engine_step_tokens_per_s", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random bf16 weights and KV)",
             "config": {"workload": "C4 engine step, Mistral-7B shape (32 layers, d_model 4096, 32/8 heads, "
@@ -793,12 +808,18 @@ def run_c4(args):
                                  "per step); cpu_reference = the restated reference sampler (oracle, 1 thread) "
                                  f"timed on {n_cpu} rows and scaled to all rows, plus the logits D2H it needs"},
             "clocks": clk}
-    print(json.dumps(line), flush=True)
     ctx.close()
+    return line
 
 
 def run_decode_loop(args):
-    """--workload decode-loop: steady-state decode steps of the Mistral-7B-shaped
+    """--workload decode-loop: the decode-loop line (measure_decode_loop)."""
+    line = measure_decode_loop(args.steps, args.warmup)
+    print(json.dumps(line), flush=True)
+
+
+def measure_decode_loop(steps, warmup):
+    """Steady-state decode steps of the Mistral-7B-shaped
     decoder through the device-resident loop (zl_decode_graph), replayed as a
     CUDA graph and, for comparison, as the same launches issued eagerly.
     Rows 32 and 248 (contexts U{1024..8192}, random bf16 KV and weights); a step
@@ -812,7 +833,7 @@ def run_decode_loop(args):
     cfg = DecoderConfig.mistral_7b()
     rng = np.random.default_rng(505)
     R = 248
-    steps, warm = args.steps, args.warmup
+    warm = warmup
     lens = rng.integers(1024, 8193, size=R).astype(np.int32)
     extra = (steps + warm) * 2 + 4  # every row runs all steps of both modes and both sizes
     mb = int((lens.max() + extra * 2 + BS - 1) // BS) + 1
@@ -870,8 +891,8 @@ def run_decode_loop(args):
                                    "zl_decode_graph: rows with contexts U[1024,8192], greedy / top-k+top-p / "
                                    "top-p+repetition sampling; inputs larger than L2"},
             "modes": res}
-    print(json.dumps(line), flush=True)
     ctx.close()
+    return line
 
 
 def load_peaks():
