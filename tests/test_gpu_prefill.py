@@ -37,9 +37,12 @@ def test_f32_prefill(ctx, oracle, shape, causal):
         assert rel_err(got[r], ref[r]) <= 1e-4
 
 
+@pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("lens", [[1, 127, 128, 129], [300, 700, 5, 1024], [2000]])
-def test_bf16_prefill_d128(ctx, oracle, lens):
-    """bf16, head_dim 128, GQA 32/8: the tensor-core path (tcgen05) when it applies."""
+def test_bf16_prefill_d128(ctx, oracle, lens, causal):
+    """bf16, head_dim 128, GQA 32/8: the tensor-core path (tcgen05) when it applies,
+    causal and full (non-causal: every tile of the sequence, the last one masked
+    past the sequence end)."""
     import torch
     import zealot_b200 as zb
     H, Hkv, d = 32, 8, 128
@@ -50,10 +53,47 @@ def test_bf16_prefill_d128(ctx, oracle, lens):
     tv, v32 = bf16_tensor(oracle, v)
     out = torch.full_like(tq, float("nan"))
     zb.CudaAttention(ctx).forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d,
-                                      max(lens), causal=True)
+                                      max(lens), causal=causal)
     ctx.check_status()
-    ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=True, num_threads=8)
+    ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=causal, num_threads=8)
     assert np.max(np.abs(to_f32(out) - ref)) <= 2e-2
+
+
+def test_bf16_prefill_back_to_back_launches(ctx, oracle):
+    """The persistent kernel takes its work items from a device counter that the
+    last CTA of each launch returns to zero: launches of different sizes back to
+    back on one stream (and one after a launch whose malformed cu_seqlens was
+    reported) must each cover all of their items."""
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = 32, 8, 128
+    attn = zb.CudaAttention(ctx)
+    cases = [[1500, 40, 777], [129], [300, 2048, 5, 64, 900]]
+    runs = []
+    for i, lens in enumerate(cases):
+        rng = np.random.default_rng(100 + i)
+        cu, q, k, v = _case(rng, lens, H, Hkv, d)
+        (tq, q32), (tk, k32), (tv, v32) = (bf16_tensor(oracle, x) for x in (q, k, v))
+        runs.append((lens, cu, tq, tk, tv, q32, k32, v32))
+    outs = []
+    for rep in range(2):
+        for lens, cu, tq, tk, tv, *_ in runs:
+            out = torch.full_like(tq, float("nan"))
+            attn.forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d, max(lens), causal=True)
+            outs.append(out)
+        if rep == 0:  # a reported launch in between: sequence 1 ends past total_tokens
+            lens, cu, tq, tk, tv, *_ = runs[0]
+            bad = cu.copy()
+            bad[2] = bad[-1] + 100
+            attn.forward_gpu(tq, tk, tv, torch.from_numpy(bad).cuda(), torch.empty_like(tq), H, Hkv, d,
+                             max(lens) + 100, causal=True)
+            with pytest.raises(zb.OobBlockError):
+                ctx.check_status()
+    ctx.check_status()
+    for r, (lens, cu, tq, tk, tv, q32, k32, v32) in enumerate(runs):
+        ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=True, num_threads=8)
+        for out in (outs[r], outs[len(runs) + r]):
+            assert np.max(np.abs(to_f32(out) - ref)) <= 2e-2
 
 
 def test_bf16_prefill_c3_sampled(ctx, oracle):
