@@ -72,7 +72,12 @@ typedef struct {
 /* ----------------------------------------------------------------- context */
 
 /* Replaces GpuContext::new (src/gpu_context.rs:30-52): binds a device and
- * creates the library state. cfg may be NULL (device 0). */
+ * creates the library state. cfg may be NULL (device 0). A context is used
+ * from one host thread at a time (as gpu_context.rs:23-26), and its kernels
+ * share its workspace and counters (split-KV partials and merge counts of the
+ * decode, the persistent prefill's work counter): calls on one context whose
+ * kernels may run at the same time on different streams race. Use one
+ * context per stream that runs attention concurrently with another. */
 zl_status zl_ctx_create(const zl_ctx_cfg* cfg, zl_ctx** out);
 zl_status zl_ctx_destroy(zl_ctx* ctx);
 /* Context flags (zl_ctx_set_flags). No reference counterpart.
