@@ -81,6 +81,43 @@ def test_bf16_ragged_many_segments(ctx, oracle):
         assert np.max(np.abs(got - ref)) <= BF16_ATOL
 
 
+def test_bf16_repeatable_across_launches(ctx, oracle):
+    """Long ragged ranges (about 30 blocks per warp, most segments split over warps),
+    sentinels at several depths, empty sequences, five launches in a row: the merge
+    order is fixed by the flat split, so every launch gives the same bytes, and the
+    merge counters come back to zero each time."""
+    import torch
+    import zealot_b200 as zb
+    rng = np.random.default_rng(77)
+    H, Hkv, d, bs = 32, 8, 128, 16
+    lens = rng.integers(1500, 4000, size=16).astype(np.int64)
+    lens[[3, 11]] = 0
+    nblk = int(((lens + bs - 1) // bs).sum())
+    q, kp, vp, table, lens = decode_case(rng, len(lens), lens, H, Hkv, d, bs, nblk + 16)
+    table[5, 40] = -1
+    table[9, 2] = -1
+    table[13, 150] = -1
+    attn = zb.CudaAttention(ctx)
+    tq, q32 = bf16_tensor(oracle, q)
+    tk, k32 = bf16_tensor(oracle, kp)
+    tv, v32 = bf16_tensor(oracle, vp)
+    tt = torch.from_numpy(table).cuda()
+    tl = torch.from_numpy(np.asarray(lens, np.int32)).cuda()
+    ref = oracle.paged_decode(q32, k32, v32, table, lens, H, Hkv, d, bs, kp.shape[0], num_threads=8)
+    outs = []
+    for _ in range(5):
+        out = torch.full_like(tq, float("nan"))
+        attn.paged_forward(tq, tk, tv, tt, tl, out, len(lens), H, Hkv, d, bs, table.shape[1],
+                           num_blocks=kp.shape[0])
+        ctx.check_status()
+        got = to_f32(out)
+        assert np.max(np.abs(got - ref)) <= BF16_ATOL
+        outs.append(got)
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
+    assert np.all(outs[0][3] == 0) and np.all(outs[0][11] == 0)
+
+
 def test_bf16_c2_full(ctx, oracle):
     """Config C2 at full size: B=64, 32/8 heads, d=128, ctx U[512, 4096], block tables a
     seeded random permutation of a 65536-block pool. The pools are drawn on the GPU; the
