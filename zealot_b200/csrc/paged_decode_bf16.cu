@@ -522,7 +522,9 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
   // carry_trunc across chunks, and the first item's earlier entries are
   // scanned once.
   const int32_t* const tables = a.block_tables;
-  int ch_base = -32, ch_y = 0, ch_nv = 0;
+  // ch_end: one past the current chunk's last item; p_hi: one past the last
+  // item produced (a timed-out warp drains up to it)
+  int ch_base = -32, ch_end = 0, ch_y = 0, ch_nv = 0, p_hi = 0;
   int carry_seg = -1, carry_trunc = 0;
   if (nwork > 0) {
     int b, kvh, j;
@@ -588,13 +590,16 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     carry_seg = __shfl_sync(0xffffffffu, seg, last);
     carry_trunc = __shfl_sync(0xffffffffu, trunc ? 1 : 0, last);
     ch_base = cbase;
+    ch_end = min(cbase + 32, nwork);
     ch_y = y;
     ch_nv = nv;
   };
   // Issue the loads of item i of this warp into its ring slot (all lanes
   // call; lane 0 issues).
   auto produce = [&](int i) {
-    if (i >= ch_base + 32) build_chunk(i & ~31);
+    if (i >= nwork) return;
+    if (i >= ch_end) build_chunk(i & ~31);
+    p_hi = i + 1;
     const int src = i - ch_base;
     const int y = __shfl_sync(0xffffffffu, ch_y, src);
     const int nvalid = __shfl_sync(0xffffffffu, ch_nv, src);
@@ -838,8 +843,8 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
           }
         }
         __syncwarp();
-        if (i + STAGES < nwork) produce(i + STAGES);
-        if (two && i + 1 + STAGES < nwork) produce(i + 1 + STAGES);
+        produce(i + STAGES);
+        if (two) produce(i + 1 + STAGES);
         __syncwarp();
         i += step;
       }
@@ -996,7 +1001,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
 
   if (timed_out) {
     // Drain the loads this warp still has in flight (bounded) before exit.
-    for (int k = i_fail; k < min(nwork, i_fail + STAGES); k++) {
+    for (int k = i_fail; k < p_hi; k++) {
       const int slot = k % STAGES;
       if (!mbar_wait_warp(smem_u32(&wbars[slot]), (uint32_t)((k / STAGES) & 1), a.status)) break;
     }
