@@ -548,24 +548,38 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     carry_trunc = __any_sync(0xffffffffu, neg) ? 1 : 0;
     carry_seg = b * Hkv + kvh;
   }
+  // A chunk's table entries and lengths are fetched one chunk ahead (the f_
+  // registers) and resolved when the producer reaches the chunk, so the
+  // loads' latency hides behind the current chunk's 32 items.
+  int f_seg = -1, f_e = 0, f_b = 0, f_kvh = 0, f_j = 0, f_len = 0, f_beg = 0;
+  bool f_wneg = false;
+  auto fetch_chunk = [&](int cbase) {
+    const int idx = cbase + lane;
+    f_seg = -1; f_e = 0; f_b = 0; f_kvh = 0; f_j = 0; f_len = 0; f_beg = 0;
+    f_wneg = false;
+    if (idx < nwork) {
+      int b, kvh, j;
+      locate(item_flat(idx), b, kvh, j);
+      f_seg = b * Hkv + kvh;
+      const int32_t* tb = tables + (int64_t)b * a.max_blocks;
+      const int t = table_base(b) + j;  // table index from here on
+      f_e = tb[t];
+      // the other warps' blocks between this warp's previous item and this one
+      for (int u = 1; u < istride; u++)
+        if (j >= u) f_wneg |= tb[t - u] < 0;
+      f_len = a.seq_lens[b];  // issued with the table reads: one latency, not two
+      if constexpr (PARTIAL) f_beg = a.tok_begin ? a.tok_begin[b] : 0;
+      f_b = b;
+      f_kvh = kvh;
+      f_j = t;
+    }
+  };
   auto build_chunk = [&](int cbase) {
     const int idx = cbase + lane;
     const bool ok = idx < nwork;
-    int seg = -1, e = 0, b = 0, kvh = 0, j = 0, len = 0, beg = 0;
-    bool wneg = false;
-    if (ok) {
-      locate(item_flat(idx), b, kvh, j);
-      seg = b * Hkv + kvh;
-      const int32_t* tb = tables + (int64_t)b * a.max_blocks;
-      const int t = table_base(b) + j;  // table index from here on
-      e = tb[t];
-      // the other warps' blocks between this warp's previous item and this one
-      for (int u = 1; u < istride; u++)
-        if (j >= u) wneg |= tb[t - u] < 0;
-      len = a.seq_lens[b];  // issued with the table reads: one latency, not two
-      if constexpr (PARTIAL) beg = a.tok_begin ? a.tok_begin[b] : 0;
-      j = t;
-    }
+    const int seg = f_seg, e = f_e, b = f_b, kvh = f_kvh, j = f_j, len = f_len, beg = f_beg;
+    const bool wneg = f_wneg;
+    (void)b; (void)beg;
     const unsigned negm = __ballot_sync(0xffffffffu, ok && (e < 0 || wneg));
     const int prev = __shfl_up_sync(0xffffffffu, seg, 1);
     const unsigned startm = __ballot_sync(0xffffffffu, lane == 0 || seg != prev);
@@ -593,6 +607,7 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     ch_end = min(cbase + 32, nwork);
     ch_y = y;
     ch_nv = nv;
+    if (cbase + 32 < nwork) fetch_chunk(cbase + 32);
   };
   // Issue the loads of item i of this warp into its ring slot (all lanes
   // call; lane 0 issues).
@@ -621,7 +636,10 @@ paged_decode_bf16_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap
     }
   };
 
-  if (nwork > 0) build_chunk(0);  // the first 32 items' table entries
+  if (nwork > 0) {  // the first 32 items' table entries (and the next 32 fetched)
+    fetch_chunk(0);
+    build_chunk(0);
+  }
   griddep_wait();  // K/V, q and the outputs belong to the stream order from here on
   {
     const int pre = min(nwork, STAGES);
