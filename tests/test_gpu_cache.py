@@ -8,8 +8,11 @@ from helpers import bf16_tensor, f32_tensor
 pytestmark = pytest.mark.gpu
 
 
+# Shapes: 16-byte chunks per token row of 8, 128, 18, 256 (block size 12, not a
+# power of two) and 512 on the vector form; 20-byte rows on the element form.
 @pytest.mark.parametrize("dtype,Hkv,d,bs", [("f32", 4, 8, 16), ("bf16", 8, 128, 16),
-                                            ("bf16", 2, 72, 8), ("f32", 3, 5, 4)])
+                                            ("bf16", 2, 72, 8), ("bf16", 8, 256, 12),
+                                            ("f32", 16, 128, 16), ("f32", 3, 5, 4)])
 def test_reshape_and_cache_bit_exact(ctx, oracle, dtype, Hkv, d, bs):
     import torch
     import zealot_b200 as zb
