@@ -259,6 +259,10 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
         const int st1 = (gj + 1) & 1;
         const uint32_t ph1 = ((gj + 1) >> 1) & 1;
         if (!(ok = mbar_wait(bar(V_FULL + st), ph, a.status))) break;
+        // The next tile's K usually landed long ago: probed here, while P of
+        // head 0 is still being written, a completed K needs no wait between
+        // head 0's P V and its next scores.
+        bool k_next = j + 1 < nkv && mbar_test(bar(K_FULL + st1), ph1);
         for (int w = 0; w < NQ && ok; w++) {
           if (!(ok = mbar_wait(bar(P_READY + w), gj & 1, a.status))) break;
           // the first P V of an item overwrites O: the previous item's epilogue must have read it
@@ -267,7 +271,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmQ,
           issue_pv(w, st, j > 0);
           if (w == NQ - 1) tc_commit(bar(V_EMPTY + st));
           if (j + 1 < nkv) {
-            if (w == 0 && !(ok = mbar_wait(bar(K_FULL + st1), ph1, a.status))) break;
+            if (w == 0 && !k_next && !(ok = mbar_wait(bar(K_FULL + st1), ph1, a.status))) break;
             tc_fence_after();
             issue_s(w, st1);
             tc_commit(bar(S_FULL + w));
