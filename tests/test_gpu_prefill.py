@@ -152,6 +152,30 @@ def test_bf16_prefill_max_moves_inside_tiles(ctx, oracle):
     assert np.max(np.abs(to_f32(out) - ref)) <= 2e-2
 
 
+def test_bf16_prefill_max_moves_in_first_tile(ctx, oracle):
+    """Keys scaled far above the rest in the first key tile of each sequence (both
+    64-key halves): every query tile past the diagonal meets them in its first
+    tile, where the running max is set, and again through the O rescale of the
+    later tiles never being needed. Rows are checked against the oracle."""
+    import torch
+    import zealot_b200 as zb
+    H, Hkv, d = 32, 8, 128
+    rng = np.random.default_rng(31)
+    lens = [600, 333]
+    cu, q, k, v = _case(rng, lens, H, Hkv, d)
+    for pos, factor in ((64 + 36, 30.0), (64 + 63, 20.0), (600 + 5, 15.0), (600 + 64 + 5, 40.0)):
+        k[pos] *= factor
+    tq, q32 = bf16_tensor(oracle, q)
+    tk, k32 = bf16_tensor(oracle, k)
+    tv, v32 = bf16_tensor(oracle, v)
+    out = torch.full_like(tq, float("nan"))
+    zb.CudaAttention(ctx).forward_gpu(tq, tk, tv, torch.from_numpy(cu).cuda(), out, H, Hkv, d,
+                                      max(lens), causal=True)
+    ctx.check_status()
+    ref = oracle.prefill_varlen(q32, k32, v32, cu, H, Hkv, d, causal=True, num_threads=8)
+    assert np.max(np.abs(to_f32(out) - ref)) <= 2e-2
+
+
 @pytest.mark.parametrize("path", ["tcgen05", "generic"])
 @pytest.mark.parametrize("bad", ["past_end", "backwards", "longer_than_max"])
 def test_malformed_cu_seqlens_is_reported(ctx, oracle, path, bad):
