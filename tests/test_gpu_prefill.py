@@ -154,9 +154,10 @@ def test_bf16_prefill_max_moves_inside_tiles(ctx, oracle):
 
 def test_bf16_prefill_max_moves_in_first_tile(ctx, oracle):
     """Keys scaled far above the rest in the first key tile of each sequence (both
-    64-key halves): every query tile past the diagonal meets them in its first
-    tile, where the running max is set, and again through the O rescale of the
-    later tiles never being needed. Rows are checked against the oracle."""
+    64-key halves): every query tile past the diagonal sets its running max from
+    them in its first tile, and no later tile comes near it, so the exponentials
+    of all later tiles are taken far below the max. Rows are checked against the
+    oracle."""
     import torch
     import zealot_b200 as zb
     H, Hkv, d = 32, 8, 128
